@@ -1,0 +1,182 @@
+"""Generate golden vectors by running the reference implementation itself.
+
+Run in a checkout that has the reference tree (not on the GPU box):
+
+    python tests/golden/make_golden.py --reference /path/to/llima
+
+It imports ``sima_lmm.gguf.gguf_conversion`` from the reference (with a stub for the
+unused ``llama_cpp`` import, ``gguf_conversion.py:7``), feeds seeded synthetic GGUF
+bytes through the reference's own ``unpack_gguf_tensor`` (``gguf_conversion.py:102-176``),
+gguf-py's ``dequantize`` (the force_float path, ``:171-172``) and
+``GgufModel._permute_qk_proj`` (``:314-332``), and writes one ``.npz`` per case into
+this directory.  The requantization warning the reference logs
+(``ggml_quant.py:879-880``) is captured as text.  Library versions are recorded in
+``versions.json``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import logging
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+
+from llima_b200.formats import FORMATS          # noqa: E402
+from llima_b200.synth import gen_tensor_bytes   # noqa: E402
+
+
+class _Capture(logging.Handler):
+    def __init__(self):
+        super().__init__(logging.WARNING)
+        self.messages: list[str] = []
+
+    def emit(self, record):
+        self.messages.append(record.getMessage())
+
+
+def _edge_kquant(fmt: str, n_sb: int, seed: int) -> np.ndarray:
+    """K-quant super-blocks that hit the corner cases of the requantization:
+    zero scales, zero mins, both zero, d = 0, dmin = 0, negative and subnormal f16
+    constants, extreme ratios that clip, and all-equal codes."""
+    f = FORMATS[fmt]
+    rng = np.random.default_rng(seed)
+    u = gen_tensor_bytes(fmt, n_sb * 256, seed).reshape(n_sb, f.unit_bytes).copy()
+    if fmt == "Q6_K":
+        # int8 sub-scales over the whole range, zero and negative d, subnormal d
+        u[:, 192:208] = rng.integers(-128, 128, size=(n_sb, 16), dtype=np.int8).view(np.uint8)
+        d = u[:, 208:210].copy().view(np.float16)
+        d[0::7] = 0
+        d[1::7] = -d[1::7]
+        d[2::7] = np.float16(3e-7)          # subnormal f16
+        d[3::7] = np.float16(60000.0)       # products overflow f16 -> inf
+        u[:, 208:210] = d.view(np.uint8)
+        return u.reshape(-1)
+    d = u[:, 0:2].copy().view(np.float16)
+    dmin = u[:, 2:4].copy().view(np.float16)
+    sc_bytes = u[:, 4:16]
+    for i in range(n_sb):
+        case = i % 12
+        if case == 0:
+            sc_bytes[i] = 0                      # all scales and mins zero
+        elif case == 1:
+            d[i] = 0                             # S = 0 -> alternative scale
+        elif case == 2:
+            dmin[i] = 0                          # M = 0 (negated: -0.0)
+        elif case == 3:
+            d[i] = np.float16(1e-7)              # tiny S, large |r| -> sf < 1
+            dmin[i] = np.float16(0.5)
+        elif case == 4:
+            d[i] = -d[i]                         # negative scale
+        elif case == 5:
+            dmin[i] = -dmin[i]                   # negative min (positive M)
+        elif case == 6:
+            d[i] = np.float16(6e-8)              # smallest subnormal
+        elif case == 7:
+            dmin[i] = np.float16(65504.0)        # M overflows f16 -> -inf
+        elif case == 8:
+            u[i, 16:] = 0xFF                     # all codes at the top
+        elif case == 9:
+            u[i, 16:] = 0x00                     # all codes zero
+        elif case == 10:
+            d[i] = np.float16(1e-4)
+            dmin[i] = np.float16(1e-4)
+            sc_bytes[i] = 0x41                   # equal small scales and mins
+    u[:, 0:2] = d.view(np.uint8)
+    u[:, 2:4] = dmin.view(np.uint8)
+    return u.reshape(-1)
+
+
+def _nonfinite(fmt: str, n_units: int, seed: int) -> np.ndarray:
+    """Fully uniform random bytes: f16 constants include NaN, inf and huge values."""
+    f = FORMATS[fmt]
+    rng = np.random.default_rng(seed)
+    return np.frombuffer(rng.bytes(n_units * f.unit_bytes), dtype=np.uint8).copy()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--out", default=str(HERE))
+    args = ap.parse_args()
+
+    sys.path.insert(0, args.reference)
+    sys.modules.setdefault("llama_cpp", types.SimpleNamespace(Llama=object))
+    import gguf
+    import ml_dtypes
+    from gguf import GGMLQuantizationType as T
+    from gguf import dequantize as gguf_dequantize
+    from sima_lmm.gguf import gguf_conversion as gc
+
+    cap = _Capture()
+    logging.getLogger("sima_lmm.gguf.ggml_quant").addHandler(cap)
+    out = Path(args.out)
+    manifest = []
+
+    def run(case: str, fmt: str, raw: np.ndarray, rows: int, cols: int, heads: int = 0):
+        f = FORMATS[fmt]
+        n_units = rows * cols // f.unit_values
+        assert raw.size == n_units * f.unit_bytes
+        data = raw.reshape(rows, -1) if fmt not in ("F32",) else raw.view(np.float32).reshape(rows, cols)
+        tensor = types.SimpleNamespace(tensor_type=getattr(T, fmt), data=data,
+                                       shape=np.array([cols, rows], dtype=np.uint64))
+        cap.messages.clear()
+        with np.errstate(all="ignore"):
+            scales, codes = gc.unpack_gguf_tensor(tensor, False)
+        warning = "\n".join(cap.messages)
+        with np.errstate(all="ignore"):
+            f32 = np.asarray(gguf_dequantize(data, getattr(T, fmt)), dtype=np.float32).reshape(rows, cols)
+        rec = {"raw": raw, "rows": rows, "cols": cols, "fmt": fmt,
+               "codes": codes.view(np.uint8) if codes.dtype == ml_dtypes.int4 else codes,
+               "codes_dtype": str(codes.dtype), "f32": f32, "warning": warning}
+        if scales is not None:
+            rec["scales"] = scales
+        if heads:
+            ps, pw = gc.GgufModel._permute_qk_proj(None, scales, codes, heads)
+            rec["perm_heads"] = heads
+            rec["perm_codes"] = pw.view(np.uint8) if pw.dtype == ml_dtypes.int4 else pw
+            if ps is not None:
+                rec["perm_scales"] = ps
+        np.savez_compressed(out / f"{case}.npz", **rec)
+        manifest.append({"case": case, "fmt": fmt, "rows": rows, "cols": cols,
+                         "heads": heads, "warning": bool(warning)})
+
+    shapes = {"Q8_0": [(37, 64), (6, 4096)], "Q4_0": [(37, 64), (6, 4096)],
+              "Q4_K": [(37, 256), (5, 4096)], "Q5_K": [(37, 256), (5, 4096)],
+              "Q6_K": [(37, 256), (5, 4096)]}
+    for fmt, shp in shapes.items():
+        for seed in (0, 1, 2):
+            for rows, cols in shp:
+                raw = gen_tensor_bytes(fmt, rows * cols, 1000 * seed + rows)
+                run(f"{fmt}_seed{seed}_{rows}x{cols}", fmt, raw, rows, cols)
+        run(f"{fmt}_single_unit", fmt, gen_tensor_bytes(fmt, FORMATS[fmt].unit_values, 77),
+            1, FORMATS[fmt].unit_values)
+        run(f"{fmt}_nonfinite", fmt, _nonfinite(fmt, 96 if FORMATS[fmt].unit_values == 256 else 384, 5),
+            12 if FORMATS[fmt].unit_values == 256 else 48, 2048 if FORMATS[fmt].unit_values == 256 else 256)
+    for fmt in ("Q4_K", "Q5_K", "Q6_K"):
+        run(f"{fmt}_edges", fmt, _edge_kquant(fmt, 96, 11), 24, 1024)
+    # q/k head permutation of a llama-style model: 4 heads of dim 16, and 2 kv heads
+    run("Q4_K_perm_q", "Q4_K", gen_tensor_bytes("Q4_K", 64 * 512, 21), 64, 512, heads=4)
+    run("Q6_K_perm_k", "Q6_K", gen_tensor_bytes("Q6_K", 32 * 512, 22), 32, 512, heads=2)
+    run("Q8_0_perm_q", "Q8_0", gen_tensor_bytes("Q8_0", 64 * 128, 23), 64, 128, heads=4)
+    run("F32_norm", "F32", gen_tensor_bytes("F32", 1000, 24, "norm"), 1000, 1)
+
+    versions = {"numpy": np.__version__, "ml_dtypes": ml_dtypes.__version__,
+                "gguf": getattr(gguf, "__version__", None) or _dist_version("gguf"),
+                "reference": "sima-neat/llima 0.6.2", "cases": manifest}
+    (out / "versions.json").write_text(json.dumps(versions, indent=1) + "\n")
+    print(f"wrote {len(manifest)} cases to {out}")
+
+
+def _dist_version(name: str):
+    from importlib.metadata import version
+    return version(name)
+
+
+if __name__ == "__main__":
+    main()
