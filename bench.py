@@ -1,0 +1,462 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 GGUF weight-preparation path.
+
+One step converts a whole model-shaped GGUF tensor set (default: the Llama-3-8B
+Q4_K_M-shaped set, 291 tensors, 5.31 GB of GGUF bytes) into the reference's integer
+layout (int8/int4 codes + f32 block scales).  With N GPUs (torchrun, one process per
+GPU) the tensors are sharded by bytes across the ranks with no collective on the data
+path; the model stays the same, so scaling is strong (fixed total work).
+
+Printed (rank 0, one JSON line): whole-job GGUF GB/s with inputs resident in HBM
+(`value`), seconds per model, the end-to-end number through the C ABI host-buffer call
+(`gq_convert_host`, pinned host input -> pinned host output, copies inside the timed
+region), the roofline of the dominant kernel, SM clocks sampled during the timed region,
+and the CPU baseline (the numpy oracle on the host cores, rank 0 at N=1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--model llama3-8b] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GGUF weight GB/s dequant+requant (frac. of HBM peak) and s/model at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--model", default="llama3-8b", choices=["llama3-8b", "qwen2.5-7b", "llama3-70b"])
+    ap.add_argument("--out", default="codes", choices=["codes", "f32", "both"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------------------
+# CPU side: the numpy oracle, timed on the host cores (spawned workers)
+# ---------------------------------------------------------------------------------------
+
+def _cpu_worker(model, seed, rank, sample_mb, seconds, passes, barrier, queue):
+    import numpy as np  # noqa: F401
+    sys.path.insert(0, str(ROOT))
+    from llima_b200.synth import gen_tensor_bytes, model_specs
+    from oracle import ggml_oracle as O
+
+    # A slice of the model with its format mix: whole rows of every quantized format,
+    # in proportion to the bytes each format holds in the model.
+    specs = [s for s in model_specs(model, seed) if s.fmt != "F32"]
+    by_fmt: dict[str, int] = {}
+    for s in specs:
+        by_fmt[s.fmt] = by_fmt.get(s.fmt, 0) + s.nbytes
+    total = sum(by_fmt.values())
+    sample = []
+    for fmt, nb in sorted(by_fmt.items()):
+        f = O.FORMATS[fmt]
+        share = sample_mb * (1 << 20) * nb / total
+        units = max(1, int(share // f.unit_bytes))
+        n_values = units * f.unit_values
+        raw = gen_tensor_bytes(fmt, n_values, seed * 7919 + rank * 31 + len(sample))
+        sample.append((fmt, raw.tobytes(), n_values))
+    nbytes = sum(len(r) for _, r, _ in sample)
+    barrier.wait()
+    t0 = time.time()
+    done = 0
+    n_pass = 0
+    while True:
+        for fmt, raw, n_values in sample:
+            O.unpack_tensor(fmt, raw, (n_values // 256 if n_values % 256 == 0 else n_values // 32,
+                                       256 if n_values % 256 == 0 else 32), log=False)
+        done += nbytes
+        n_pass += 1
+        if (passes and n_pass >= passes) or (not passes and time.time() - t0 >= seconds):
+            break
+    queue.put((done, t0, time.time()))
+
+
+def cpu_throughput(model, seed, cores, sample_mb=8.0, seconds=8.0, passes=0):
+    """GB/s of GGUF bytes converted by `cores` spawned processes running the oracle."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    barrier = ctx.Barrier(cores)
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_cpu_worker, args=(model, seed, r, sample_mb, seconds, passes, barrier, queue))
+             for r in range(cores)]
+    for p in procs:
+        p.start()
+    res = [queue.get() for _ in procs]
+    for p in procs:
+        p.join()
+    total = sum(r[0] for r in res)
+    wall = max(r[2] for r in res) - min(r[1] for r in res)
+    return total / wall / 1e9, total, wall
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]):
+        self.gpus = set(gpus)
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait()
+        self.file.flush()
+        self.file.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in self.gpus:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.file.name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_per_byte(kernel: str):
+    """DRAM bytes per algorithmic byte of `kernel`, from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return float(json.loads(p.read_text())[kernel]["dram_bytes_per_algorithmic_byte"])
+    except (KeyError, ValueError, TypeError):
+        return None
+
+
+def workload_config(args, world) -> dict:
+    from llima_b200.formats import output_layout
+    from llima_b200.synth import model_specs
+    specs = model_specs(args.model, args.seed)
+    gguf = sum(s.nbytes for s in specs)
+    out = 0
+    for s in specs:
+        lay = output_layout(s.fmt, s.n_values)
+        if lay["codes"] == 0:
+            out += lay["values"]
+        else:
+            out += (lay["codes"] + lay["scales"] if args.out in ("codes", "both") else 0) + \
+                (lay["values"] if args.out in ("f32", "both") else 0)
+    return {"workload": f"{args.model} GGUF tensor set, whole model per step", "model": args.model,
+            "n_tensors": len(specs), "gguf_bytes": gguf, "out_bytes": out, "output": args.out,
+            "parallelism": f"tensor-shard x{world}",
+            "l2": "inputs larger than L2 (GGUF bytes >> 126 MB), no flush"}
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from llima_b200 import _native as N
+    from llima_b200.device import DeviceBatch, DeviceTensor, alloc_outputs
+    from llima_b200.formats import FORMATS
+    from llima_b200.shard import piece_cost, plan_shards
+    from llima_b200.synth import gen_tensor_bytes_torch, head_count_for, model_specs
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    out_mask = {"codes": N.OUT_CODES, "f32": N.OUT_F32, "both": N.OUT_CODES | N.OUT_F32}[args.out]
+    N.lib()   # fail loudly before any work if the library is missing
+
+    specs = model_specs(args.model, args.seed)
+    plan = plan_shards([(s.fmt, s.rows, s.cols, head_count_for(args.model, s.name) > 0) for s in specs],
+                       world, args.out)
+    mine = plan[rank]
+    tensors: list[DeviceTensor] = []
+    by_index: dict[int, list] = {}
+    for p in mine:
+        by_index.setdefault(p.index, []).append(p)
+    for idx, plist in by_index.items():
+        s = specs[idx]
+        full = gen_tensor_bytes_torch(s.fmt, s.n_values, s.seed, dev, s.kind)
+        f = FORMATS[s.fmt]
+        row_bytes = s.cols // f.unit_values * f.unit_bytes
+        for p in plist:
+            src = full[p.row0 * row_bytes:p.row1 * row_bytes].clone()
+            heads = head_count_for(args.model, s.name) if p.rows == s.rows else 0
+            t = DeviceTensor(s.fmt, p.rows, s.cols, src, heads, name=s.name)
+            tensors.append(alloc_outputs(t, out_mask))
+        del full
+    torch.cuda.synchronize()
+
+    order = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "F32"]
+    batches = {}
+    for fmt in order:
+        ts = [t for t in tensors if t.fmt == fmt]
+        if ts:
+            batches[fmt] = DeviceBatch(ts, out_mask)
+    algo = {fmt: sum(piece_cost(fmt, t.rows, t.cols, args.out) for t in b.tensors) for fmt, b in batches.items()}
+    gguf_bytes = sum(t.src_bytes for t in tensors)
+    out_bytes = sum(t.out_bytes for t in tensors)
+    launches_per_step = sum(-(-len(b.tensors) // 256) for b in batches.values())
+
+    stream = torch.cuda.current_stream()
+    ev = {fmt: [] for fmt in batches}
+
+    def step(record: bool):
+        for fmt, b in batches.items():
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                b.run(stream, reset_diag=False)
+                e1.record(stream)
+                ev[fmt].append((e0, e1))
+            else:
+                b.run(stream, reset_diag=False)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for b in batches.values():
+        b.run(stream, reset_diag=True)
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    barrier()
+    sampler = ClockSampler([local_rank] if world == 1 else list(range(world))) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize()
+    barrier()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms_total = t_start.elapsed_time(t_end)
+    per_fmt_ms = {fmt: sum(a.elapsed_time(b) for a, b in lst) / len(lst) for fmt, lst in ev.items()}
+    if world > 1:
+        t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+
+    # correctness guard on the timed buffers: the diagnostics of the asymmetric formats
+    # must have been written (rounding error of random data is > 0)
+    diag_ok = True
+    for fmt in ("Q4_K", "Q5_K"):
+        if fmt in batches and out_mask & N.OUT_CODES:
+            diag_ok &= bool((batches[fmt].diags[:, 0] != 0).any().item())
+
+    # ---- end to end through the C ABI host-buffer call (pinned host memory)
+    e2e = None
+    if not args.no_e2e and args.e2e_steps > 0:
+        import ctypes
+        host_src = []
+        host_out = []
+        recs = (N.Tensor * len(tensors))()
+        for i, t in enumerate(tensors):
+            hs = torch.empty(t.src.numel(), dtype=torch.uint8, pin_memory=True)
+            hs.copy_(t.src)
+            host_src.append(hs)
+            r = N.Tensor()
+            r.type = FORMATS[t.fmt].type_id
+            r.perm_heads = t.perm_heads
+            r.rows, r.cols = t.rows, t.cols
+            r.src, r.src_bytes = hs.data_ptr(), hs.numel()
+            outs = {}
+            for name in ("codes", "scales", "values"):
+                dt = getattr(t, name)
+                if dt is not None:
+                    ht = torch.empty(dt.shape, dtype=dt.dtype, pin_memory=True)
+                    outs[name] = ht
+                    setattr(r, name, ht.data_ptr())
+            host_out.append(outs)
+            recs[i] = r
+        diags = (N.Diag * len(tensors))()
+        sess = ctypes.c_void_p()
+        N.check(N.lib().gq_session_create(local_rank, 1 << 30, ctypes.byref(sess)), "gq_session_create")
+        N.check(N.lib().gq_convert_host(sess, recs, len(tensors), out_mask, diags), "gq_convert_host")  # warm-up
+        barrier()
+        times = []
+        for _ in range(args.e2e_steps):
+            barrier()
+            t0 = time.perf_counter()
+            N.check(N.lib().gq_convert_host(sess, recs, len(tensors), out_mask, diags), "gq_convert_host")
+            times.append(time.perf_counter() - t0)
+        barrier()
+        e2e_s = sum(times) / len(times)
+        if world > 1:
+            t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        # the host results must equal the device-resident results
+        same = True
+        for t, outs in zip(tensors, host_out):
+            for name, ht in outs.items():
+                same &= bool(torch.equal(ht.to(dev, non_blocking=False).view(torch.uint8),
+                                         getattr(t, name).view(torch.uint8)))
+        N.lib().gq_session_destroy(sess)
+        h2d = sum(h.numel() for h in host_src)
+        d2h = sum(ht.numel() * ht.element_size() for outs in host_out for ht in outs.values())
+        agg = torch.tensor([float(gguf_bytes), float(h2d), float(d2h), 1.0 if same else 0.0], dtype=torch.float64,
+                           device=dev)
+        if world > 1:
+            dist.all_reduce(agg, op=dist.ReduceOp.SUM)
+        e2e = {"value": float(agg[0].item()) / e2e_s / 1e9, "unit": "GB/s", "s_per_model": e2e_s,
+               "h2d_bytes_per_step": int(agg[1].item()), "d2h_bytes_per_step": int(agg[2].item()),
+               "matches_device": bool(agg[3].item() == world), "api": "gq_convert_host (pinned host buffers)"}
+        del host_src, host_out
+
+    tot = torch.tensor([float(gguf_bytes), float(out_bytes), 1.0 if diag_ok else 0.0], dtype=torch.float64,
+                       device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    all_gguf, all_out = float(tot[0].item()), float(tot[1].item())
+    if rank != 0:
+        return None
+
+    peak, peak_kind = measured_peak()
+    dom = max(per_fmt_ms, key=lambda f: per_fmt_ms[f])
+    achieved = algo[dom] / (per_fmt_ms[dom] / 1e3) / 1e9
+    tpb = traffic_per_byte(f"{dom.lower()}_convert")
+    roofline = {"bound": "hbm", "kernel": f"gq_convert_kernel<{dom}>", "achieved": round(achieved, 1),
+                "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "traffic": None if tpb is None else int(tpb * algo[dom]),
+                "algorithmic_bytes_per_launch": algo[dom],
+                "per_format_ms": {k: round(v, 4) for k, v in per_fmt_ms.items()},
+                "per_format_GBps": {k: round(algo[k] / (v / 1e3) / 1e9, 1) for k, v in per_fmt_ms.items()}}
+    value = all_gguf / (ms_step / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "s_per_model": round(ms_step / 1e3, 6),
+        "hbm_frac_whole_step": round((all_gguf + all_out) / (ms_step / 1e3) / 1e9 / (peak * world), 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8->int8 (f32 requant)",
+        "data": "synthetic (seeded, BASELINE distributions)",
+        "config": workload_config(args, world),
+        "roofline": roofline, "gpu_launches": launches_per_step * args.steps, "diag_written": bool(tot[2].item() == world),
+        "e2e": e2e, "clocks": clocks,
+    }
+    return line
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world != 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        cores = host_cores()
+        vals = []
+        for i in range(args.warmup + args.steps):
+            gbs, total, wall = cpu_throughput(args.model, args.seed, cores, sample_mb=4.0, passes=1)
+            if i >= args.warmup:
+                vals.append((gbs, total, wall))
+        value = statistics.median(v[0] for v in vals)
+        sample = f"per step: {cores} spawned workers x 4 MB slice of the {args.model} format mix, one pass each"
+        line = {"metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(statistics.median(v[2] for v in vals) * 1e3, 2),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "u8->int8 (f32 requant)", "data": "synthetic (seeded, BASELINE distributions)",
+                "config": workload_config(args, args.gpus),
+                "impl": "reference",
+                "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+    try:
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            # before any CUDA work: spawned workers, bounded by --cpu-seconds
+            cores = host_cores()
+            gbs, total, wall = cpu_throughput(args.model, args.seed, cores, sample_mb=8.0,
+                                              seconds=args.cpu_seconds)
+            cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                   "sample": f"{cores} spawned workers, each an 8 MB slice of the {args.model} format mix "
+                             f"converted repeatedly for {args.cpu_seconds:.0f} s ({total / 1e9:.2f} GB in {wall:.1f} s)"}
+        line = run_ours(args, rank, world, local_rank)
+        if rank == 0 and line is not None:
+            line["cpu_baseline"] = cpu
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

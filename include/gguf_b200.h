@@ -1,0 +1,152 @@
+/*
+ * gguf_b200.h - C ABI of the B200 GGUF weight-preparation library (libgguf_b200.so).
+ *
+ * The library turns GGUF block-quantized tensor bytes into the integer weight layout
+ * LLiMa's model compiler hands to the Modalix compile step, on NVIDIA B200 (sm_100a):
+ *
+ *   Q8_0 -> f32 block scales (per 32) + int8 codes            (unpack_q8_0)
+ *   Q4_0 -> f32 block scales (per 32) + int4 codes, 1 byte each (unpack_q4, SYMMETRIC)
+ *   Q4_K, Q5_K -> f32 scales (per 32) + int8 codes, through the asymmetric -> symmetric
+ *                 requantization (unpack_k_quant + convert_to_simple_block_quant)
+ *   Q6_K -> f32 scales (per 16) + int8 codes                   (same path, no requant)
+ *   F32 / F16 / BF16 -> copied unchanged
+ *
+ * and, on request, into f32 values exactly as gguf-py's dequantize computes them (the
+ * reference's force_float path).  Results are bit-identical to the reference's numpy
+ * path.  Reference interfaces replaced, in sima-neat/llima 0.6.2:
+ *
+ *   gq_convert / gq_convert_batch   sima_lmm/gguf/gguf_conversion.py:102-176
+ *                                   (unpack_gguf_tensor), with the q/k head permutation of
+ *                                   GgufModel._permute_qk_proj (gguf_conversion.py:314-332)
+ *                                   fused into the output indexing
+ *   gq_requantize_symmetric         sima_lmm/gguf/ggml_quant.py:785-886 (requantize_symmetric)
+ *   gq_query                        sizes implied by ggml_quant.py:104-131 (format table)
+ *   gq_convert_host                 the same as gq_convert_batch, on host buffers
+ *
+ * Conventions: every function returns GQ_OK (0) or a negative GQ_ERR_* code and never
+ * aborts; gq_strerror() describes a code.  Device pointers are plain CUDA device
+ * addresses of the current device; `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  Work is enqueued on `stream` and the call returns without waiting, except
+ * gq_convert_host which returns when its results are in host memory.
+ */
+#ifndef GGUF_B200_H
+#define GGUF_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GQ_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define GQ_API __attribute__((visibility("default")))
+#else
+#define GQ_API
+#endif
+
+/* status codes */
+#define GQ_OK 0
+#define GQ_ERR_TYPE (-1)      /* GGML type not handled by this path */
+#define GQ_ERR_SIZE (-2)      /* sizes inconsistent with the type's block geometry */
+#define GQ_ERR_ALIGN (-3)     /* a pointer is not aligned as required */
+#define GQ_ERR_NULL (-4)      /* a pointer the requested outputs need is NULL */
+#define GQ_ERR_ARG (-5)       /* other invalid argument (mode, count, head count) */
+#define GQ_ERR_CUDA (-6)      /* CUDA runtime error; see gq_last_cuda_error() */
+#define GQ_ERR_NOMEM (-7)     /* device or pinned host allocation failed */
+
+/* GGML type ids: the numbers of QuantizationMode, sima_lmm/gguf/ggml_quant.py:9-26 */
+#define GQ_TYPE_F32 0
+#define GQ_TYPE_F16 1
+#define GQ_TYPE_Q4_0 2
+#define GQ_TYPE_Q8_0 8
+#define GQ_TYPE_Q4_K 12
+#define GQ_TYPE_Q5_K 13
+#define GQ_TYPE_Q6_K 14
+#define GQ_TYPE_BF16 30
+
+/* outputs (bit mask) */
+#define GQ_OUT_CODES 1        /* f32 block scales + integer codes (force_float=False) */
+#define GQ_OUT_F32 2          /* f32 values as gguf-py dequantize computes them (force_float=True) */
+
+/* Requantization diagnostics of one tensor, accumulated as maxima over its blocks.
+ * ggml_quant.py:866-880 computes the same two numbers and logs a warning when
+ * clip_err > 0 or round_err > 0.5. */
+typedef struct gq_diag {
+    uint32_t round_err_bits;  /* bit pattern of the f32 max |int16(rint(r*sf)) - r*sf| (NaN wins) */
+    int32_t clip_err;         /* max |clip(q') - q'| */
+} gq_diag_t;
+
+/* One tensor to convert.  Shape is (rows, cols) as unpack_gguf_tensor returns it (the
+ * reversed GGUF dims); cols must be a multiple of the type's block (32, or 256 for K). */
+typedef struct gq_tensor {
+    int32_t type;             /* GQ_TYPE_* */
+    int32_t perm_heads;       /* >0: apply the llama q/k row permutation for this many heads */
+    int64_t rows;
+    int64_t cols;
+    const void* src;          /* GGUF bytes of the tensor, 16-byte aligned */
+    size_t src_bytes;         /* must be >= the tensor's GGUF size */
+    void* codes;              /* GQ_OUT_CODES: rows*cols bytes, 16-byte aligned */
+    float* scales;            /* GQ_OUT_CODES: rows*cols/block floats (block 32, Q6_K 16) */
+    float* values;            /* GQ_OUT_F32: rows*cols floats, 16-byte aligned; float types:
+                                 the unchanged copy (rows*cols elements of the type) */
+    gq_diag_t* diag;          /* optional; Q4_K/Q5_K with GQ_OUT_CODES accumulate into it */
+} gq_tensor_t;
+
+/* Sizes of one tensor's input and outputs. */
+typedef struct gq_layout {
+    int64_t n_values;
+    int64_t n_units;          /* stored blocks / super-blocks */
+    int64_t src_bytes;
+    int64_t codes_bytes;
+    int64_t scales_count;     /* f32 block scales */
+    int64_t values_bytes;     /* f32 output (or the float copy) */
+    int32_t block_values;     /* values per output scale: 32, 16, or 0 for float types */
+    int32_t unit_values;      /* values per stored unit: 1, 32 or 256 */
+} gq_layout_t;
+
+GQ_API int gq_version(void);
+GQ_API const char* gq_strerror(int status);
+/* CUDA error code (cudaError_t) behind the last GQ_ERR_CUDA of the calling thread. */
+GQ_API int gq_last_cuda_error(void);
+
+GQ_API int gq_query(int32_t type, int64_t rows, int64_t cols, gq_layout_t* out);
+
+/* Zero `count` diagnostics records (device memory) on `stream`. */
+GQ_API int gq_diag_reset(gq_diag_t* diag, int32_t count, void* stream);
+
+/* Convert one tensor (device buffers).  Replaces unpack_gguf_tensor
+ * (gguf_conversion.py:102-176) plus, when perm_heads > 0, _permute_qk_proj (:314-332).
+ * The tensor's diag, if any, is zeroed first. */
+GQ_API int gq_convert(const gq_tensor_t* tensor, int32_t out_mask, void* stream);
+
+/* Convert `count` tensors (device buffers) with one kernel launch per GGML type present.
+ * Diagnostics accumulate (max) into each tensor's diag: zero them beforehand. */
+GQ_API int gq_convert_batch(const gq_tensor_t* tensors, int32_t count, int32_t out_mask, void* stream);
+
+/* requantize_symmetric (ggml_quant.py:785-886) as a standalone scheme:
+ * block_consts (n_blocks, 2) f32 [scale, min]; codes (n_blocks, block) int8 unsigned values;
+ * out: scales (n_blocks) f32 and codes (n_blocks, block) in [-2^(bits-1), 2^(bits-1)-1].
+ * block must be 1..256 and output_bits 2..8.  All device pointers. */
+GQ_API int gq_requantize_symmetric(const float* block_consts, const int8_t* codes, int64_t n_blocks,
+                            int32_t block, int32_t output_bits, float* out_scales,
+                            int8_t* out_codes, gq_diag_t* diag, void* stream);
+
+/* Host-buffer path: an opaque per-device session owning device staging memory and
+ * streams.  gq_convert_host copies each tensor's bytes host->device, converts and copies
+ * the results device->host, pipelining tensors (and pieces of large tensors) across two
+ * staging slots; host buffers may be pinned (fastest) or pageable.  The pointers in
+ * `tensors` are HOST pointers; diags (optional, host, one per tensor) receive the maxima. */
+typedef struct gq_session gq_session_t;
+GQ_API int gq_session_create(int32_t device, size_t staging_bytes, gq_session_t** out);
+GQ_API int gq_session_destroy(gq_session_t* session);
+GQ_API int gq_convert_host(gq_session_t* session, const gq_tensor_t* tensors, int32_t count,
+                    int32_t out_mask, gq_diag_t* host_diags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GGUF_B200_H */

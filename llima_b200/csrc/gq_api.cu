@@ -1,0 +1,481 @@
+// C ABI of libgguf_b200.so: argument validation, batching by GGML type, and the
+// host-buffer session that pipelines host->device copies, kernels and device->host copies.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <vector>
+
+#include "gq_internal.h"
+
+namespace {
+
+thread_local int g_last_cuda = 0;
+
+int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return GQ_OK;
+    g_last_cuda = static_cast<int>(e);
+    return GQ_ERR_CUDA;
+}
+int cuda_status(int e) { return cuda_status(static_cast<cudaError_t>(e)); }
+
+struct TypeInfo {
+    int unit_values;
+    int unit_bytes;
+    int block_values;   // 0 for float types
+    bool asym;
+};
+
+bool type_info(int type, TypeInfo* ti) {
+    switch (type) {
+        case GQ_TYPE_F32: *ti = {1, 4, 0, false}; return true;
+        case GQ_TYPE_F16: *ti = {1, 2, 0, false}; return true;
+        case GQ_TYPE_BF16: *ti = {1, 2, 0, false}; return true;
+        case GQ_TYPE_Q4_0: *ti = {32, 18, 32, false}; return true;
+        case GQ_TYPE_Q8_0: *ti = {32, 34, 32, false}; return true;
+        case GQ_TYPE_Q4_K: *ti = {256, 144, 32, true}; return true;
+        case GQ_TYPE_Q5_K: *ti = {256, 176, 32, true}; return true;
+        case GQ_TYPE_Q6_K: *ti = {256, 210, 16, false}; return true;
+        default: return false;
+    }
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+bool valid_mask(int m) { return m == GQ_OUT_CODES || m == GQ_OUT_F32 || m == (GQ_OUT_CODES | GQ_OUT_F32); }
+
+// Sizes, and the checks that need no pointers.
+int shape_check(const gq_tensor_t& t, TypeInfo* ti, int64_t* n_values, int64_t* n_units) {
+    if (!type_info(t.type, ti)) return GQ_ERR_TYPE;
+    if (t.rows < 0 || t.cols < 0) return GQ_ERR_SIZE;
+    if (t.cols != 0 && t.rows > INT64_MAX / t.cols) return GQ_ERR_SIZE;
+    const int64_t nv = t.rows * t.cols;
+    if (t.cols % ti->unit_values != 0) return GQ_ERR_SIZE;
+    if (t.perm_heads < 0) return GQ_ERR_ARG;
+    if (t.perm_heads > 0 && (t.rows % (2 * static_cast<int64_t>(t.perm_heads)) != 0)) return GQ_ERR_ARG;
+    *n_values = nv;
+    *n_units = nv / ti->unit_values;
+    const int64_t need = *n_units * ti->unit_bytes;
+    if (static_cast<uint64_t>(need) > t.src_bytes) return GQ_ERR_SIZE;
+    return GQ_OK;
+}
+
+int validate(const gq_tensor_t& t, int out_mask, TypeInfo* ti, int64_t* n_values, int64_t* n_units) {
+    const int st = shape_check(t, ti, n_values, n_units);
+    if (st != GQ_OK) return st;
+    if (*n_values == 0) return GQ_OK;
+    if (t.src == nullptr) return GQ_ERR_NULL;
+    if (!aligned(t.src, 16)) return GQ_ERR_ALIGN;
+    if (ti->block_values == 0) {
+        if (t.values == nullptr) return GQ_ERR_NULL;
+        if (!aligned(t.values, 16)) return GQ_ERR_ALIGN;
+        return GQ_OK;
+    }
+    if (out_mask & GQ_OUT_CODES) {
+        if (t.codes == nullptr || t.scales == nullptr) return GQ_ERR_NULL;
+        if (!aligned(t.codes, 16) || !aligned(t.scales, 4)) return GQ_ERR_ALIGN;
+        if (t.diag != nullptr && !aligned(t.diag, 4)) return GQ_ERR_ALIGN;
+    }
+    if (out_mask & GQ_OUT_F32) {
+        if (t.values == nullptr) return GQ_ERR_NULL;
+        if (!aligned(t.values, 16)) return GQ_ERR_ALIGN;
+    }
+    return GQ_OK;
+}
+
+gq::GqDesc make_desc(const gq_tensor_t& t, const TypeInfo& ti, int64_t n_units) {
+    gq::GqDesc d{};
+    d.src = static_cast<const uint8_t*>(t.src);
+    d.codes = static_cast<uint8_t*>(t.codes);
+    d.scales = t.scales;
+    d.values = t.values;
+    d.diag = t.diag;
+    d.n_units = n_units;
+    d.units_per_row = t.cols / ti.unit_values;
+    d.perm_heads = t.perm_heads;
+    d.rows_per_head = t.perm_heads > 0 ? static_cast<int32_t>(t.rows / t.perm_heads) : 0;
+    return d;
+}
+
+// Launch one kernel per GGML type present (the tensors are already validated).
+int launch_grouped(const std::vector<std::pair<gq::GqDesc, int>>& items, int out_mask, void* stream) {
+    static const int kTypes[] = {GQ_TYPE_Q4_K, GQ_TYPE_Q6_K, GQ_TYPE_Q5_K, GQ_TYPE_Q8_0,
+                                 GQ_TYPE_Q4_0, GQ_TYPE_F32, GQ_TYPE_F16, GQ_TYPE_BF16};
+    std::unique_ptr<gq::GqBatch> b(new (std::nothrow) gq::GqBatch);
+    if (!b) return GQ_ERR_NOMEM;
+    for (int type : kTypes) {
+        // F16 and BF16 are both 2-byte copies: launch them together
+        if (type == GQ_TYPE_BF16) continue;
+        auto same = [type](int t) { return t == type || (type == GQ_TYPE_F16 && t == GQ_TYPE_BF16); };
+        b->n = 0;
+        b->total_tiles = 0;
+        for (size_t i = 0; i <= items.size(); ++i) {
+            const bool last = i == items.size();
+            if (!last && same(items[i].second)) {
+                gq::GqDesc d = items[i].first;
+                d.tile_begin = b->total_tiles;
+                b->total_tiles += gq::tiles_for(type, d.n_units);
+                b->d[b->n++] = d;
+            }
+            if ((last || b->n == gq::kMaxDesc) && b->n > 0) {
+                const int e = gq::launch_batch(type, out_mask, *b, stream);
+                if (e != 0) return cuda_status(e);
+                b->n = 0;
+                b->total_tiles = 0;
+            }
+        }
+    }
+    return GQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gq_version(void) { return GQ_ABI_VERSION; }
+
+const char* gq_strerror(int status) {
+    switch (status) {
+        case GQ_OK: return "success";
+        case GQ_ERR_TYPE: return "GGML type not supported by this path";
+        case GQ_ERR_SIZE: return "sizes do not match the type's block geometry";
+        case GQ_ERR_ALIGN: return "pointer not aligned as required";
+        case GQ_ERR_NULL: return "a required pointer is NULL";
+        case GQ_ERR_ARG: return "invalid argument";
+        case GQ_ERR_CUDA: return "CUDA runtime error";
+        case GQ_ERR_NOMEM: return "out of memory";
+        default: return "unknown status";
+    }
+}
+
+int gq_last_cuda_error(void) { return g_last_cuda; }
+
+int gq_query(int32_t type, int64_t rows, int64_t cols, gq_layout_t* out) {
+    if (out == nullptr) return GQ_ERR_NULL;
+    gq_tensor_t t{};
+    t.type = type;
+    t.rows = rows;
+    t.cols = cols;
+    t.src_bytes = SIZE_MAX;
+    TypeInfo ti;
+    int64_t nv = 0, nu = 0;
+    const int st = shape_check(t, &ti, &nv, &nu);
+    if (st != GQ_OK) return st;
+    out->n_values = nv;
+    out->n_units = nu;
+    out->src_bytes = nu * ti.unit_bytes;
+    out->block_values = ti.block_values;
+    out->unit_values = ti.unit_values;
+    if (ti.block_values == 0) {
+        out->codes_bytes = 0;
+        out->scales_count = 0;
+        out->values_bytes = nv * ti.unit_bytes;
+    } else {
+        out->codes_bytes = nv;
+        out->scales_count = nv / ti.block_values;
+        out->values_bytes = 4 * nv;
+    }
+    return GQ_OK;
+}
+
+int gq_diag_reset(gq_diag_t* diag, int32_t count, void* stream) {
+    if (count < 0) return GQ_ERR_ARG;
+    if (count == 0) return GQ_OK;
+    if (diag == nullptr) return GQ_ERR_NULL;
+    return cuda_status(cudaMemsetAsync(diag, 0, sizeof(gq_diag_t) * count, static_cast<cudaStream_t>(stream)));
+}
+
+int gq_convert_batch(const gq_tensor_t* tensors, int32_t count, int32_t out_mask, void* stream) {
+    if (count < 0) return GQ_ERR_ARG;
+    if (count > 0 && tensors == nullptr) return GQ_ERR_NULL;
+    if (!valid_mask(out_mask)) return GQ_ERR_ARG;
+    std::vector<std::pair<gq::GqDesc, int>> items;
+    items.reserve(count);
+    for (int i = 0; i < count; ++i) {
+        TypeInfo ti;
+        int64_t nv = 0, nu = 0;
+        const int st = validate(tensors[i], out_mask, &ti, &nv, &nu);
+        if (st != GQ_OK) return st;
+        if (nv == 0) continue;
+        items.emplace_back(make_desc(tensors[i], ti, nu), tensors[i].type);
+    }
+    return launch_grouped(items, out_mask, stream);
+}
+
+int gq_convert(const gq_tensor_t* tensor, int32_t out_mask, void* stream) {
+    if (tensor == nullptr) return GQ_ERR_NULL;
+    if (!valid_mask(out_mask)) return GQ_ERR_ARG;
+    TypeInfo ti;
+    int64_t nv = 0, nu = 0;
+    const int st = validate(*tensor, out_mask, &ti, &nv, &nu);
+    if (st != GQ_OK) return st;
+    if (tensor->diag != nullptr && ti.asym && (out_mask & GQ_OUT_CODES)) {
+        const int e = gq_diag_reset(tensor->diag, 1, stream);
+        if (e != GQ_OK) return e;
+    }
+    return gq_convert_batch(tensor, 1, out_mask, stream);
+}
+
+int gq_requantize_symmetric(const float* block_consts, const int8_t* codes, int64_t n_blocks,
+                            int32_t block, int32_t output_bits, float* out_scales,
+                            int8_t* out_codes, gq_diag_t* diag, void* stream) {
+    if (n_blocks < 0 || block < 1 || block > 256 || output_bits < 2 || output_bits > 8) return GQ_ERR_ARG;
+    if (diag != nullptr) {
+        const int e = gq_diag_reset(diag, 1, stream);
+        if (e != GQ_OK) return e;
+    }
+    if (n_blocks == 0) return GQ_OK;
+    if (!block_consts || !codes || !out_scales || !out_codes) return GQ_ERR_NULL;
+    if (!aligned(block_consts, 4) || !aligned(out_scales, 4)) return GQ_ERR_ALIGN;
+    return cuda_status(gq::launch_requant(block_consts, codes, n_blocks, block, output_bits, out_scales,
+                                          out_codes, diag, stream));
+}
+
+// ---------------------------------------------------------------------------------------
+// Host-buffer session
+// ---------------------------------------------------------------------------------------
+
+struct gq_session {
+    int device = 0;
+    size_t slot_bytes = 0;
+    uint8_t* slot[2] = {nullptr, nullptr};
+    cudaStream_t stream[2] = {nullptr, nullptr};
+    gq_diag_t* d_diag = nullptr;
+    int diag_cap = 0;
+};
+
+namespace {
+
+constexpr size_t kAlign = 256;
+size_t round_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
+
+// Device bytes one unit of a tensor occupies in a staging slot.
+size_t unit_footprint(const TypeInfo& ti, int out_mask) {
+    size_t b = ti.unit_bytes;
+    if (ti.block_values == 0) return b + ti.unit_bytes;
+    if (out_mask & GQ_OUT_CODES) b += ti.unit_values + 4 * (ti.unit_values / ti.block_values);
+    if (out_mask & GQ_OUT_F32) b += 4 * static_cast<size_t>(ti.unit_values);
+    return b;
+}
+
+struct Member {
+    int tensor;
+    int64_t unit0;
+    int64_t units;
+};
+
+int guard_device(int device) {
+    int cur = -1;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_status(e);
+    if (cur != device) return cuda_status(cudaSetDevice(device));
+    return GQ_OK;
+}
+
+}  // namespace
+
+int gq_session_create(int32_t device, size_t staging_bytes, gq_session_t** out) {
+    if (out == nullptr) return GQ_ERR_NULL;
+    *out = nullptr;
+    if (staging_bytes < (1u << 20)) return GQ_ERR_ARG;
+    int st = guard_device(device);
+    if (st != GQ_OK) return st;
+    std::unique_ptr<gq_session> s(new (std::nothrow) gq_session);
+    if (!s) return GQ_ERR_NOMEM;
+    s->device = device;
+    s->slot_bytes = staging_bytes & ~(kAlign - 1);
+    for (int i = 0; i < 2; ++i) {
+        if (cudaMalloc(&s->slot[i], s->slot_bytes) != cudaSuccess) {
+            gq_session_destroy(s.release());
+            cudaGetLastError();
+            return GQ_ERR_NOMEM;
+        }
+        if (cudaStreamCreateWithFlags(&s->stream[i], cudaStreamNonBlocking) != cudaSuccess) {
+            const int e = cuda_status(cudaGetLastError());
+            gq_session_destroy(s.release());
+            return e;
+        }
+    }
+    *out = s.release();
+    return GQ_OK;
+}
+
+int gq_session_destroy(gq_session_t* s) {
+    if (s == nullptr) return GQ_OK;
+    cudaSetDevice(s->device);
+    for (int i = 0; i < 2; ++i) {
+        if (s->stream[i]) cudaStreamSynchronize(s->stream[i]);
+    }
+    for (int i = 0; i < 2; ++i) {
+        if (s->stream[i]) cudaStreamDestroy(s->stream[i]);
+        if (s->slot[i]) cudaFree(s->slot[i]);
+    }
+    if (s->d_diag) cudaFree(s->d_diag);
+    delete s;
+    return GQ_OK;
+}
+
+int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, int32_t out_mask,
+                    gq_diag_t* host_diags) {
+    if (s == nullptr) return GQ_ERR_NULL;
+    if (count < 0) return GQ_ERR_ARG;
+    if (count > 0 && tensors == nullptr) return GQ_ERR_NULL;
+    if (!valid_mask(out_mask)) return GQ_ERR_ARG;
+    int st = guard_device(s->device);
+    if (st != GQ_OK) return st;
+
+    std::vector<TypeInfo> info(count);
+    std::vector<int64_t> units(count);
+    for (int i = 0; i < count; ++i) {
+        int64_t nv = 0;
+        // host pointers: alignment of the host copy source does not matter
+        gq_tensor_t t = tensors[i];
+        st = shape_check(t, &info[i], &nv, &units[i]);
+        if (st != GQ_OK) return st;
+        if (nv == 0) continue;
+        if (t.src == nullptr) return GQ_ERR_NULL;
+        if (info[i].block_values == 0) {
+            if (t.values == nullptr) return GQ_ERR_NULL;
+        } else {
+            if ((out_mask & GQ_OUT_CODES) && (t.codes == nullptr || t.scales == nullptr)) return GQ_ERR_NULL;
+            if ((out_mask & GQ_OUT_F32) && t.values == nullptr) return GQ_ERR_NULL;
+        }
+        // a permuted tensor moves rows across its whole extent: it must fit one slot
+        if (t.perm_heads > 0 &&
+            round_up(units[i] * unit_footprint(info[i], out_mask)) + 4 * kAlign > s->slot_bytes)
+            return GQ_ERR_SIZE;
+    }
+    if (host_diags != nullptr && count > s->diag_cap) {
+        if (s->d_diag) cudaFree(s->d_diag);
+        s->d_diag = nullptr;
+        s->diag_cap = 0;
+        if (cudaMalloc(&s->d_diag, sizeof(gq_diag_t) * count) != cudaSuccess) {
+            cudaGetLastError();
+            return GQ_ERR_NOMEM;
+        }
+        s->diag_cap = count;
+    }
+    if (host_diags != nullptr && count > 0) {
+        st = cuda_status(cudaMemsetAsync(s->d_diag, 0, sizeof(gq_diag_t) * count, s->stream[0]));
+        if (st != GQ_OK) return st;
+        // the second stream must not run its kernels before the zeroing
+        cudaEvent_t ev;
+        if ((st = cuda_status(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming))) != GQ_OK) return st;
+        cudaEventRecord(ev, s->stream[0]);
+        cudaStreamWaitEvent(s->stream[1], ev, 0);
+        cudaEventDestroy(ev);
+    }
+
+    // Cut the work into pieces that fill a slot: large tensors are split on unit
+    // boundaries, small ones are packed together.
+    std::vector<std::vector<Member>> pieces;
+    {
+        std::vector<Member> cur;
+        size_t used = 0;
+        for (int i = 0; i < count; ++i) {
+            int64_t done = 0;
+            const size_t fp = unit_footprint(info[i], out_mask);
+            while (done < units[i]) {
+                const size_t room = s->slot_bytes > used + 4 * kAlign ? s->slot_bytes - used - 4 * kAlign : 0;
+                int64_t take = static_cast<int64_t>(room / fp);
+                if (tensors[i].perm_heads > 0 && take < units[i]) take = 0;
+                if (take <= 0) {
+                    if (cur.empty()) return GQ_ERR_SIZE;
+                    pieces.push_back(std::move(cur));
+                    cur.clear();
+                    used = 0;
+                    continue;
+                }
+                take = std::min<int64_t>(take, units[i] - done);
+                cur.push_back({i, done, take});
+                used += round_up(take * fp) + 4 * kAlign;
+                done += take;
+            }
+        }
+        if (!cur.empty()) pieces.push_back(std::move(cur));
+    }
+
+    std::vector<std::pair<gq::GqDesc, int>> items;
+    for (size_t p = 0; p < pieces.size(); ++p) {
+        const int k = static_cast<int>(p & 1);
+        cudaStream_t stream = s->stream[k];
+        uint8_t* base = s->slot[k];
+        size_t off = 0;
+        items.clear();
+        struct Out { void* host; const void* dev; size_t bytes; };
+        std::vector<Out> outs;
+        for (const Member& m : pieces[p]) {
+            const gq_tensor_t& t = tensors[m.tensor];
+            const TypeInfo& ti = info[m.tensor];
+            const size_t src_bytes = static_cast<size_t>(m.units) * ti.unit_bytes;
+            uint8_t* dsrc = base + off;
+            off = round_up(off + src_bytes);
+            st = cuda_status(cudaMemcpyAsync(dsrc, static_cast<const uint8_t*>(t.src) + m.unit0 * ti.unit_bytes,
+                                             src_bytes, cudaMemcpyHostToDevice, stream));
+            if (st != GQ_OK) return st;
+            gq_tensor_t dt = t;
+            dt.rows = t.perm_heads > 0 ? t.rows : m.units * ti.unit_values / t.cols;
+            dt.src = dsrc;
+            dt.src_bytes = src_bytes;
+            dt.diag = host_diags ? s->d_diag + m.tensor : nullptr;
+            const int64_t nvals = m.units * ti.unit_values;
+            if (ti.block_values == 0) {
+                const size_t vb = static_cast<size_t>(nvals) * ti.unit_bytes;
+                dt.values = reinterpret_cast<float*>(base + off);
+                off = round_up(off + vb);
+                outs.push_back({static_cast<uint8_t*>(static_cast<void*>(t.values)) + m.unit0 * ti.unit_bytes,
+                                dt.values, vb});
+            } else {
+                if (out_mask & GQ_OUT_CODES) {
+                    dt.codes = base + off;
+                    off = round_up(off + nvals);
+                    dt.scales = reinterpret_cast<float*>(base + off);
+                    const int64_t nsc = nvals / ti.block_values;
+                    off = round_up(off + 4 * nsc);
+                    outs.push_back({static_cast<uint8_t*>(t.codes) + m.unit0 * ti.unit_values, dt.codes,
+                                    static_cast<size_t>(nvals)});
+                    outs.push_back({t.scales + m.unit0 * (ti.unit_values / ti.block_values), dt.scales,
+                                    static_cast<size_t>(4 * nsc)});
+                }
+                if (out_mask & GQ_OUT_F32) {
+                    dt.values = reinterpret_cast<float*>(base + off);
+                    off = round_up(off + 4 * static_cast<size_t>(nvals));
+                    outs.push_back({t.values + m.unit0 * ti.unit_values, dt.values, static_cast<size_t>(4 * nvals)});
+                }
+            }
+            // rows of a piece: whole rows are not required (rows only matter for the
+            // permutation, which keeps tensors whole); present the piece as one row
+            if (t.perm_heads == 0) {
+                dt.rows = 1;
+                dt.cols = nvals;
+            }
+            items.emplace_back(make_desc(dt, ti, m.units), t.type);
+        }
+        st = launch_grouped(items, out_mask, stream);
+        if (st != GQ_OK) return st;
+        for (const Out& o : outs) {
+            st = cuda_status(cudaMemcpyAsync(o.host, o.dev, o.bytes, cudaMemcpyDeviceToHost, stream));
+            if (st != GQ_OK) return st;
+        }
+    }
+    if (host_diags != nullptr && count > 0) {
+        // both streams' kernels must finish before the maxima are read
+        cudaEvent_t ev;
+        if ((st = cuda_status(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming))) != GQ_OK) return st;
+        cudaEventRecord(ev, s->stream[1]);
+        cudaStreamWaitEvent(s->stream[0], ev, 0);
+        cudaEventDestroy(ev);
+        st = cuda_status(cudaMemcpyAsync(host_diags, s->d_diag, sizeof(gq_diag_t) * count,
+                                         cudaMemcpyDeviceToHost, s->stream[0]));
+        if (st != GQ_OK) return st;
+    }
+    for (int i = 0; i < 2; ++i) {
+        st = cuda_status(cudaStreamSynchronize(s->stream[i]));
+        if (st != GQ_OK) return st;
+    }
+    return GQ_OK;
+}
+
+}  // extern "C"

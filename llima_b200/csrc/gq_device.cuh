@@ -1,0 +1,225 @@
+// Device helpers for the GGUF conversion kernels (sm_100a).
+//
+// Exactness: every floating-point step that the reference performs in numpy f32 is
+// written with an explicitly rounded intrinsic (__fmul_rn, __fadd_rn, __fsub_rn,
+// __fdiv_rn) so that no FMA contraction or fast-math substitution can change a bit.
+// The library is also compiled with -fmad=false and without --use_fast_math (no FTZ).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "gq_internal.h"
+
+namespace gq {
+
+// ---- f16 <-> f32 ------------------------------------------------------------------
+
+__device__ __forceinline__ float h2f(uint32_t bits) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xFFFFu)));
+}
+
+// numpy's f32 -> f16 astype: round to nearest even, overflow to inf, subnormals kept.
+__device__ __forceinline__ float round_to_f16(float x) { return __half2float(__float2half_rn(x)); }
+
+// numpy float32 -> int16 on x86-64: converted through int32 (cvttss2si), which turns NaN
+// and values outside int32 into INT32_MIN; the low 16 bits are kept.
+__device__ __forceinline__ int f32_to_i16_x86(float x) {
+    if (!(fabsf(x) < 2147483648.0f)) return 0;
+    return static_cast<int>(static_cast<short>(__float2int_rz(x)));
+}
+
+// ---- per-block requantization parameters (requantize_symmetric) --------------------
+
+// f32(f16(1e-4)): SCALE_EPSILON of ggml_quant.py:836 widened exactly (f16 bits 0x068E).
+constexpr float kScaleEpsilon = 1.0001659393310547e-4f;
+
+struct Requant {
+    float sf;        // scale factor (integer-valued on the fast path)
+    int rm;          // int16(rint(r * sf))
+    float scale;     // S / sf, the output block scale
+    float round_err; // |rm - r * sf|
+    int clip_err;    // max |clip(q') - q'| over the block
+    int sfi;         // integer scale factor, valid when fast
+    bool fast;       // sf is an integer: q' = q * sfi + rm exactly
+    bool clip;       // some code of the block needs clipping
+};
+
+// ggml_quant.py:826-882 for one block with scale S, min M (already the negated f16
+// min), and the block's smallest / largest unsigned code.  Output range [lo_out, hi_out].
+__device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int qmax,
+                                                 int lo_out, int hi_out) {
+    Requant p;
+    const float s_eff = (S == 0.0f) ? ((fabsf(M) > kScaleEpsilon) ? M : kScaleEpsilon) : S;
+    const float r = __fdiv_rn(M, s_eff);
+    const float lo = __fadd_rn(static_cast<float>(qmin), r);
+    const float hi = __fadd_rn(static_cast<float>(qmax), r);
+    float sf = 16.0f;
+    // np.minimum(16, -128/lo) and np.minimum(sf, 127/hi).  Neither quotient can be NaN
+    // here (lo < 0 and hi > 0 exclude NaN), so fminf matches np.minimum.  A quotient of
+    // 16 or more cannot lower sf, so the division is skipped exactly then.
+    if (lo < static_cast<float>(lo_out) / 16.0f) sf = fminf(sf, __fdiv_rn(static_cast<float>(lo_out), lo));
+    if (hi > static_cast<float>(hi_out) / 16.0f) sf = fminf(sf, __fdiv_rn(static_cast<float>(hi_out), hi));
+    if (sf > 0.98f) sf = fmaxf(floorf(sf), 1.0f);
+    const float rmv = __fmul_rn(r, sf);
+    const int rm = f32_to_i16_x86(rintf(rmv));
+    p.sf = sf;
+    p.rm = rm;
+    p.round_err = fabsf(__fsub_rn(static_cast<float>(rm), rmv));
+    p.scale = __fdiv_rn(S, sf);
+    // q' is monotone in q (sf >= 0, |rm| < 2^10, no int16 wrap), so the block's extreme
+    // codes bound the clipping of every code.
+    const int vmin = f32_to_i16_x86(rintf(__fmul_rn(static_cast<float>(qmin), sf))) + rm;
+    const int vmax = f32_to_i16_x86(rintf(__fmul_rn(static_cast<float>(qmax), sf))) + rm;
+    p.clip = (vmax > hi_out) || (vmin < lo_out);
+    p.clip_err = max(0, max(vmax - hi_out, lo_out - vmin));
+    p.fast = (sf > 0.98f) || (sf == 0.0f);
+    p.sfi = p.fast ? static_cast<int>(sf) : 0;
+    return p;
+}
+
+// General per-value requant (non-integer scale factor).
+__device__ __forceinline__ int requant_value(int q, float sf, int rm, int lo_out, int hi_out) {
+    const int c = f32_to_i16_x86(rintf(__fmul_rn(static_cast<float>(q), sf)));
+    const int v = static_cast<int>(static_cast<short>(c + rm));
+    return min(max(v, lo_out), hi_out);
+}
+
+// Fast path on a word holding 4 unsigned codes (one per byte, each <= 31):
+// q' = q * sfi + rm computed in 16-bit lanes with a 0x4000 bias (no cross-lane carry),
+// optionally clamped, and the low bytes packed back in order.
+constexpr uint32_t kLaneBias = 0x4000u;
+
+__device__ __forceinline__ uint32_t requant_word_fast(uint32_t x, uint32_t sfi, uint32_t k2,
+                                                      bool clip, uint32_t lo2, uint32_t hi2) {
+    uint32_t e = x & 0x00FF00FFu;
+    uint32_t o = (x >> 8) & 0x00FF00FFu;
+    e = e * sfi + k2;
+    o = o * sfi + k2;
+    if (clip) {
+        e = __vminu2(__vmaxu2(e, lo2), hi2);
+        o = __vminu2(__vmaxu2(o, lo2), hi2);
+    }
+    return __byte_perm(e, o, 0x6240);
+}
+
+__device__ __forceinline__ uint32_t requant_word_slow(uint32_t x, float sf, int rm, int lo_out,
+                                                      int hi_out) {
+    uint32_t out = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const int q = (x >> (8 * b)) & 0xFF;
+        out |= (static_cast<uint32_t>(requant_value(q, sf, rm, lo_out, hi_out)) & 0xFFu) << (8 * b);
+    }
+    return out;
+}
+
+// min / max of the 4 bytes of a word
+__device__ __forceinline__ int byte_min4(uint32_t w) {
+    w = __vminu4(w, w >> 16);
+    w = __vminu4(w, w >> 8);
+    return w & 0xFF;
+}
+__device__ __forceinline__ int byte_max4(uint32_t w) {
+    w = __vmaxu4(w, w >> 16);
+    w = __vmaxu4(w, w >> 8);
+    return w & 0xFF;
+}
+
+// ---- shared memory access ------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) {
+    return *reinterpret_cast<const uint32_t*>(p);
+}
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) {
+    return *reinterpret_cast<const uint4*>(p);
+}
+__device__ __forceinline__ uint32_t lds16(const uint8_t* p) {
+    return *reinterpret_cast<const uint16_t*>(p);
+}
+
+// 16 bytes from a 2-byte-aligned shared address: five aligned words and funnel shifts.
+__device__ __forceinline__ uint4 lds128_align2(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    const uint32_t sh = static_cast<uint32_t>(a & 3u) * 8u;
+    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+    uint4 r;
+    r.x = __funnelshift_r(w0, w1, sh);
+    r.y = __funnelshift_r(w1, w2, sh);
+    r.z = __funnelshift_r(w2, w3, sh);
+    r.w = __funnelshift_r(w3, w4, sh);
+    return r;
+}
+
+// ---- global memory --------------------------------------------------------------------
+
+__device__ __forceinline__ void stg128(void* p, uint4 v) {
+    *reinterpret_cast<uint4*>(p) = v;
+}
+__device__ __forceinline__ void stg128f(float* p, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+
+// cp.async of one 16-byte chunk, reading only `src_bytes` (1..16) bytes; the rest of the
+// shared chunk is zero-filled.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n"
+                 :: "r"(smem_u32addr(smem_dst)), "l"(gmem_src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
+
+// ---- misc ------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
+
+// Output unit index after the llama q/k head permutation (gguf_conversion.py:314-332):
+// row h*D + 2a + t moves to h*D + t*D/2 + a.
+__device__ __forceinline__ int64_t permute_unit(const GqDesc& d, int64_t unit) {
+    if (d.perm_heads == 0) return unit;
+    const int64_t row = unit / d.units_per_row;
+    const int64_t col = unit - row * d.units_per_row;
+    const int64_t head = row / d.rows_per_head;
+    const int64_t i = row - head * d.rows_per_head;
+    const int64_t out_row = head * d.rows_per_head + (i & 1) * (d.rows_per_head >> 1) + (i >> 1);
+    return out_row * d.units_per_row + col;
+}
+
+// Diagnostics accumulated per warp while its tiles stay in one tensor.
+struct DiagAcc {
+    gq_diag_t* target = nullptr;
+    uint32_t round_bits = 0;
+    int clip = 0;
+
+    __device__ __forceinline__ void add(float round_err, int clip_err) {
+        round_bits = max(round_bits, __float_as_uint(fabsf(round_err)));
+        clip = max(clip, clip_err);
+    }
+    // Warp-collective: reduce over lanes and publish with atomics (skipped when it cannot
+    // raise the stored maxima).
+    __device__ __forceinline__ void flush(int lane) {
+        const uint32_t rb = __reduce_max_sync(0xffffffffu, round_bits);
+        const int ce = __reduce_max_sync(0xffffffffu, clip);
+        if (lane == 0 && target != nullptr) {
+            volatile gq_diag_t* t = target;
+            if (rb > t->round_err_bits) atomicMax(&target->round_err_bits, rb);
+            if (ce > t->clip_err) atomicMax(&target->clip_err, ce);
+        }
+        round_bits = 0;
+        clip = 0;
+    }
+    __device__ __forceinline__ void retarget(gq_diag_t* t, int lane) {
+        if (t != target) {
+            flush(lane);
+            target = t;
+        }
+    }
+};
+
+}  // namespace gq

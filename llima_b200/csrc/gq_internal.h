@@ -1,0 +1,44 @@
+// Internal types shared by the kernels and the C ABI layer.
+#pragma once
+
+#include <stdint.h>
+
+#include "../../include/gguf_b200.h"
+
+namespace gq {
+
+// One tensor of a batch launch as the kernels see it.  Work is cut into tiles of a
+// fixed number of stored units; tiles are numbered across the batch and tile_begin is
+// this tensor's first tile.
+struct GqDesc {
+    const uint8_t* src;
+    uint8_t* codes;
+    float* scales;
+    float* values;
+    gq_diag_t* diag;
+    int64_t n_units;
+    int64_t tile_begin;
+    int64_t units_per_row;   // for the head permutation
+    int32_t perm_heads;      // 0: no permutation
+    int32_t rows_per_head;   // head_dim of the permuted rows
+};
+
+// Kernel parameter block (passed by value; larger than 4 KB needs CUDA >= 12.1).
+constexpr int kMaxDesc = 256;
+
+struct GqBatch {
+    int32_t n;
+    int32_t pad;
+    int64_t total_tiles;
+    GqDesc d[kMaxDesc];
+};
+
+enum : int { kOutCodes = GQ_OUT_CODES, kOutF32 = GQ_OUT_F32 };
+
+// launch entry points implemented in gq_kernels.cu
+int launch_batch(int type, int out_mask, const GqBatch& batch, void* stream);
+int64_t tiles_for(int type, int64_t n_units);
+int launch_requant(const float* bc, const int8_t* codes, int64_t n_blocks, int block, int bits,
+                   float* out_scales, int8_t* out_codes, gq_diag_t* diag, void* stream);
+
+}  // namespace gq

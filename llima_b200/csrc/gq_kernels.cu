@@ -1,0 +1,548 @@
+// GGUF block decode + requantization kernels for B200 (sm_100a).
+//
+// One kernel per GGML format (Q8_0, Q4_0, Q4_K, Q5_K, Q6_K), a float pass-through copy,
+// and the standalone requantization scheme.  Each format kernel is a persistent grid of
+// independent warps.  A warp owns a ring of shared-memory stages and streams whole
+// tiles of stored blocks into it with 16-byte cp.async copies (the tile sizes are
+// multiples of 16 bytes, so every copy is aligned and fully coalesced), then decodes
+// the tile from shared memory:
+//
+//   * "parameter" step: one lane per output block unpacks that block's constants
+//     (6-bit scale/min, f16 super constants), scans its codes for min/max with byte-SIMD
+//     and derives the requantization parameters;
+//   * "apply" step: one lane per 16 output codes, so each warp store instruction writes
+//     512 contiguous bytes; the codes come from packed 16-bit integer arithmetic
+//     (q * sf + rm) whenever the scale factor is an integer (99.5% of blocks on the
+//     benchmark data), else from the per-value f32 formula.
+//
+// The fp32 intermediate of dequant -> requant never touches global memory.
+#include <cuda_runtime.h>
+
+#include "gq_device.cuh"
+#include "gq_internal.h"
+
+namespace gq {
+
+// ---------------------------------------------------------------------------------------
+// Format geometry: stored unit size, units per tile, pipeline depth
+// ---------------------------------------------------------------------------------------
+
+template <int TYPE>
+struct Fmt;
+
+#define GQ_FMT(TYPE, UNIT_BYTES, UNITS_PER_TILE, STAGES)                                  \
+    template <>                                                                           \
+    struct Fmt<TYPE> {                                                                    \
+        static constexpr int kUnitBytes = UNIT_BYTES;                                     \
+        static constexpr int kUnitsPerTile = UNITS_PER_TILE;                              \
+        static constexpr int kTileBytes = UNIT_BYTES * UNITS_PER_TILE;                    \
+        static constexpr int kStageBytes = kTileBytes + 16; /* slack for 20-byte reads */ \
+        static constexpr int kStages = STAGES;                                            \
+        static_assert(kTileBytes % 16 == 0, "tiles must be whole 16-byte chunks");        \
+    };
+
+GQ_FMT(GQ_TYPE_Q4_K, 144, 4, 4)   // 32 blocks of 32 per tile
+GQ_FMT(GQ_TYPE_Q5_K, 176, 4, 4)
+GQ_FMT(GQ_TYPE_Q6_K, 210, 8, 3)   // 128 blocks of 16 per tile
+GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4)   // 32 blocks of 32 per tile
+GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4)
+#undef GQ_FMT
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr unsigned kFull = 0xffffffffu;
+
+// Tensor owning global tile `t` (binary search over tile_begin).
+__device__ __forceinline__ int find_desc(const GqBatch& b, int64_t t) {
+    int lo = 0, hi = b.n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (b.d[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// Enqueue the cp.async copies of tile `t` into `stage` (nothing when t is past the end).
+template <class F>
+__device__ __forceinline__ void issue_tile(const GqBatch& b, int64_t t, uint8_t* stage, int lane) {
+    if (t >= b.total_tiles) return;
+    const GqDesc& d = b.d[find_desc(b, t)];
+    const int64_t unit0 = (t - d.tile_begin) * F::kUnitsPerTile;
+    const int64_t left = d.n_units - unit0;
+    const int nunits = left < F::kUnitsPerTile ? static_cast<int>(left) : F::kUnitsPerTile;
+    const int nbytes = nunits * F::kUnitBytes;
+    const uint8_t* src = d.src + unit0 * F::kUnitBytes;
+    for (int c = lane * 16; c < nbytes; c += 32 * 16) {
+        const int n = nbytes - c;
+        cp_async16(stage + c, src + c, n < 16 ? n : 16);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Q4_K / Q5_K: 256-value super-blocks -> 8 blocks of 32, asymmetric -> symmetric int8
+//   Q4_K: d, dmin | scales[12] | qs[128]          (ggml_quant.py:624-642)
+//   Q5_K: d, dmin | scales[12] | qh[32] | qs[128]  (ggml_quant.py:643-661)
+// ---------------------------------------------------------------------------------------
+
+template <bool Q5, int MODE>
+__device__ __forceinline__ void process_q45k(const GqDesc& D, int64_t unit0, int nunits,
+                                             const uint8_t* tile, int lane, DiagAcc& acc) {
+    constexpr int UB = Q5 ? 176 : 144;
+    constexpr int QS = Q5 ? 48 : 16;   // offset of the nibble bytes
+    constexpr int QH = 16;             // offset of the fifth-bit bytes (Q5_K)
+
+    // ---- parameter step: lane = block (super-block lane/8, sub-block lane%8)
+    const int sb = lane >> 3;
+    const int k = lane & 7;
+    const bool valid = sb < nunits;
+    const uint8_t* sbp = tile + sb * UB;
+
+    const uint32_t hdr = lds32(sbp);
+    const uint32_t s0 = lds32(sbp + 4), s1 = lds32(sbp + 8), s2 = lds32(sbp + 12);
+    int sc, mn;   // 6-bit scale / min of sub-block k (ggml_quant.py:352-375)
+    if (k < 4) {
+        sc = byte_of(s0, k) & 63;
+        mn = byte_of(s1, k) & 63;
+    } else {
+        const int j = k - 4;
+        sc = (byte_of(s2, j) & 15) | ((byte_of(s0, j) >> 6) << 4);
+        mn = (byte_of(s2, j) >> 4) | ((byte_of(s1, j) >> 6) << 4);
+    }
+    const float d = h2f(hdr);
+    const float dmin = h2f(hdr >> 16);
+
+    Requant p{};
+    if (MODE & kOutCodes) {
+        const uint8_t* qs = sbp + QS + 32 * (k >> 1);
+        const uint4 a = lds128(qs), b = lds128(qs + 16);
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        uint32_t h[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (Q5) {
+            const uint4 ha = lds128(sbp + QH), hb = lds128(sbp + QH + 16);
+            h[0] = ha.x; h[1] = ha.y; h[2] = ha.z; h[3] = ha.w;
+            h[4] = hb.x; h[5] = hb.y; h[6] = hb.z; h[7] = hb.w;
+        }
+        const int shift = 4 * (k & 1);
+        uint32_t mn4 = 0xFFFFFFFFu, mx4 = 0u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            uint32_t x = (w[i] >> shift) & 0x0F0F0F0Fu;
+            if (Q5) x |= ((h[i] >> k) & 0x01010101u) << 4;
+            mn4 = __vminu4(mn4, x);
+            mx4 = __vmaxu4(mx4, x);
+        }
+        // block constants: f16(f32 product), min negated (ggml_quant.py:771-777)
+        const float S = round_to_f16(__fmul_rn(static_cast<float>(sc), d));
+        const float M = -round_to_f16(__fmul_rn(static_cast<float>(mn), dmin));
+        p = requant_block(S, M, byte_min4(mn4), byte_max4(mx4), -128, 127);
+        if (valid) {
+            const int64_t ou = permute_unit(D, unit0 + sb);
+            D.scales[ou * 8 + k] = p.scale;
+            acc.add(p.round_err, p.clip_err);
+        }
+    }
+    // gguf-py dequantize: (d*sc)*q - dmin*m, each product rounded (Q4_K/Q5_K.dequantize_blocks)
+    const float dsc = __fmul_rn(d, static_cast<float>(sc));
+    const float dm = __fmul_rn(dmin, static_cast<float>(mn));
+
+    // ---- apply step: lane = 16 codes (chunk c of the tile: block c/2, half c%2)
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int c = 32 * r + lane;
+        const int src_lane = c >> 1;
+        float sf = 0.f;
+        int rm = 0, flags = 0;
+        if (MODE & kOutCodes) {
+            sf = __shfl_sync(kFull, p.sf, src_lane);
+            rm = __shfl_sync(kFull, p.rm, src_lane);
+            flags = __shfl_sync(kFull, (p.fast ? 1 : 0) | (p.clip ? 2 : 0) | (p.sfi << 2), src_lane);
+        }
+        float cdsc = 0.f, cdm = 0.f;
+        if (MODE & kOutF32) {
+            cdsc = __shfl_sync(kFull, dsc, src_lane);
+            cdm = __shfl_sync(kFull, dm, src_lane);
+        }
+        const int csb = c >> 4;
+        if (csb >= nunits) continue;
+        const int ck = (c >> 1) & 7;
+        const int ch = c & 1;
+        const uint8_t* base = tile + csb * UB;
+        const uint4 xv = lds128(base + QS + 32 * (ck >> 1) + 16 * ch);
+        uint32_t x[4] = {xv.x, xv.y, xv.z, xv.w};
+        const int shift = 4 * (ck & 1);
+        if (Q5) {
+            const uint4 hv = lds128(base + QH + 16 * ch);
+            const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                x[i] = ((x[i] >> shift) & 0x0F0F0F0Fu) | (((hw[i] >> ck) & 0x01010101u) << 4);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] = (x[i] >> shift) & 0x0F0F0F0Fu;
+        }
+        const int64_t ou = permute_unit(D, unit0 + csb);
+        const int64_t off = ou * 256 + 16 * (c & 15);
+        if (MODE & kOutCodes) {
+            uint4 o;
+            if (flags & 1) {
+                const uint32_t sfi = static_cast<uint32_t>(flags >> 2);
+                const uint32_t k2 = static_cast<uint32_t>(rm + static_cast<int>(kLaneBias)) * 0x00010001u;
+                const bool clip = (flags & 2) != 0;
+                constexpr uint32_t lo2 = (kLaneBias - 128u) * 0x00010001u;
+                constexpr uint32_t hi2 = (kLaneBias + 127u) * 0x00010001u;
+                o.x = requant_word_fast(x[0], sfi, k2, clip, lo2, hi2);
+                o.y = requant_word_fast(x[1], sfi, k2, clip, lo2, hi2);
+                o.z = requant_word_fast(x[2], sfi, k2, clip, lo2, hi2);
+                o.w = requant_word_fast(x[3], sfi, k2, clip, lo2, hi2);
+            } else {
+                o.x = requant_word_slow(x[0], sf, rm, -128, 127);
+                o.y = requant_word_slow(x[1], sf, rm, -128, 127);
+                o.z = requant_word_slow(x[2], sf, rm, -128, 127);
+                o.w = requant_word_slow(x[3], sf, rm, -128, 127);
+            }
+            stg128(D.codes + off, o);
+        }
+        if (MODE & kOutF32) {
+            float* dst = D.values + off;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float v[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b)
+                    v[b] = __fsub_rn(__fmul_rn(cdsc, static_cast<float>(byte_of(x[i], b))), cdm);
+                stg128f(dst + 4 * i, v[0], v[1], v[2], v[3]);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Q6_K: ql[128] | qh[64] | scales int8[16] | d  (ggml_quant.py:662-679) -> 16 blocks of 16
+// ---------------------------------------------------------------------------------------
+
+template <int MODE>
+__device__ __forceinline__ void process_q6k(const GqDesc& D, int64_t unit0, int nunits,
+                                            const uint8_t* tile, int lane) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int c = 32 * r + lane;      // block of 16 values within the tile
+        const int sb = c >> 4;
+        if (sb >= nunits) continue;
+        const int kb = c & 15;
+        const uint8_t* sbp = tile + sb * 210;
+        const float d = h2f(lds16(sbp + 208));
+        const int sc = static_cast<int>(static_cast<int8_t>(sbp[192 + kb]));
+        // value 128*hh + 32*g + j: nibble of ql[64hh + 32(g&1) + j] (low for g<2),
+        // high bits 2g..2g+1 of qh[32hh + j] (ggml_quant.py:274-308)
+        const int hh = kb >> 3, g = (kb >> 1) & 3, j0 = 16 * (kb & 1);
+        const uint4 ql = lds128_align2(sbp + 64 * hh + 32 * (g & 1) + j0);
+        const uint4 qh = lds128_align2(sbp + 128 + 32 * hh + j0);
+        const int qls = 4 * (g >> 1), qhs = 2 * g;
+        const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w};
+        const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
+        uint32_t code[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t v = ((lw[i] >> qls) & 0x0F0F0F0Fu) | (((hw[i] >> qhs) & 0x03030303u) << 4);
+            code[i] = (v + 0x60606060u) ^ 0x80808080u;   // 6-bit v - 32 as int8, per byte
+        }
+        const int64_t ou = permute_unit(D, unit0 + sb);
+        const int64_t off = ou * 256 + 16 * kb;
+        if (MODE & kOutCodes) {
+            stg128(D.codes + off, make_uint4(code[0], code[1], code[2], code[3]));
+            // block scale f16(f32(sc) * f32(d)) (ggml_quant.py:771-773), no requant (:700)
+            D.scales[ou * 16 + kb] = round_to_f16(__fmul_rn(static_cast<float>(sc), d));
+        }
+        if (MODE & kOutF32) {
+            // gguf-py Q6_K.dequantize_blocks: (d * sc) * q
+            const float dd = __fmul_rn(d, static_cast<float>(sc));
+            float* dst = D.values + off;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float v[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b)
+                    v[b] = __fmul_rn(dd, static_cast<float>(static_cast<int8_t>(byte_of(code[i], b))));
+                stg128f(dst + 4 * i, v[0], v[1], v[2], v[3]);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Q8_0: d | int8[32]   and   Q4_0: d | nibbles[16]   (ggml_quant.py:136-210)
+// ---------------------------------------------------------------------------------------
+
+template <bool Q4, int MODE>
+__device__ __forceinline__ void process_q0(const GqDesc& D, int64_t unit0, int nunits,
+                                           const uint8_t* tile, int lane) {
+    constexpr int UB = Q4 ? 18 : 34;
+    if ((MODE & kOutCodes) && lane < nunits) {
+        D.scales[permute_unit(D, unit0 + lane)] = h2f(lds16(tile + UB * lane));
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int c = 32 * r + lane;
+        const int b = c >> 1;
+        const int h = c & 1;
+        if (b >= nunits) continue;
+        const uint8_t* bp = tile + UB * b;
+        const uint4 xv = lds128_align2(bp + 2 + (Q4 ? 0 : 16 * h));
+        uint32_t x[4] = {xv.x, xv.y, xv.z, xv.w};
+        if (Q4) {
+            // value j: low nibble of byte j, value 16+j: high nibble; int4 byte = (n-8)&15 = n^8
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] = ((x[i] >> (4 * h)) & 0x0F0F0F0Fu) ^ 0x08080808u;
+        }
+        const int64_t off = permute_unit(D, unit0 + b) * 32 + 16 * h;
+        if (MODE & kOutCodes) stg128(D.codes + off, make_uint4(x[0], x[1], x[2], x[3]));
+        if (MODE & kOutF32) {
+            const float d = h2f(lds16(bp));
+            float* dst = D.values + off;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    // Q4_0: d * (n - 8); Q8_0: x * d (gguf-py dequantize_blocks)
+                    const int q = Q4 ? (static_cast<int>(((x[i] >> (8 * j)) & 0xF) ^ 8) - 8)
+                                     : static_cast<int>(static_cast<int8_t>(byte_of(x[i], j)));
+                    v[j] = Q4 ? __fmul_rn(d, static_cast<float>(q)) : __fmul_rn(static_cast<float>(q), d);
+                }
+                stg128f(dst + 4 * i, v[0], v[1], v[2], v[3]);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// The persistent per-warp pipeline shared by all block formats
+// ---------------------------------------------------------------------------------------
+
+template <int TYPE, int MODE>
+__global__ void __launch_bounds__(kThreads) gq_convert_kernel(const __grid_constant__ GqBatch batch) {
+    using F = Fmt<TYPE>;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    uint8_t* ring = smem + warp * (F::kStages * F::kStageBytes);
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+    const int64_t total = batch.total_tiles;
+
+    int64_t t_issue = first;
+#pragma unroll
+    for (int s = 0; s < F::kStages - 1; ++s) {
+        issue_tile<F>(batch, t_issue, ring + s * F::kStageBytes, lane);
+        cp_async_commit();
+        t_issue += nwarps;
+    }
+
+    DiagAcc acc;
+    int stage = 0;
+    for (int64_t t = first; t < total; t += nwarps) {
+        cp_async_wait<F::kStages - 2>();
+        __syncwarp();
+        // refill the stage consumed in the previous iteration
+        const int refill = (stage == 0) ? F::kStages - 1 : stage - 1;
+        issue_tile<F>(batch, t_issue, ring + refill * F::kStageBytes, lane);
+        cp_async_commit();
+        t_issue += nwarps;
+
+        const GqDesc& D = batch.d[find_desc(batch, t)];
+        const int64_t unit0 = (t - D.tile_begin) * F::kUnitsPerTile;
+        const int64_t left = D.n_units - unit0;
+        const int nunits = left < F::kUnitsPerTile ? static_cast<int>(left) : F::kUnitsPerTile;
+        const uint8_t* tile = ring + stage * F::kStageBytes;
+        if (TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K) {
+            if (MODE & kOutCodes) acc.retarget(D.diag, lane);
+            process_q45k<TYPE == GQ_TYPE_Q5_K, MODE>(D, unit0, nunits, tile, lane, acc);
+        } else if (TYPE == GQ_TYPE_Q6_K) {
+            process_q6k<MODE>(D, unit0, nunits, tile, lane);
+        } else {
+            process_q0<TYPE == GQ_TYPE_Q4_0, MODE>(D, unit0, nunits, tile, lane);
+        }
+        __syncwarp();
+        stage = (stage + 1 == F::kStages) ? 0 : stage + 1;
+    }
+    cp_async_wait<0>();
+    if ((TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K) && (MODE & kOutCodes)) acc.flush(lane);
+}
+
+// ---------------------------------------------------------------------------------------
+// F32 / F16 / BF16 pass-through (tile = 4096 bytes), with the head permutation for
+// 1-D bias vectors and 2-D float weights
+// ---------------------------------------------------------------------------------------
+
+constexpr int kCopyTileBytes = 4096;
+
+template <int ES>
+__global__ void __launch_bounds__(kThreads) gq_copy_kernel(const __grid_constant__ GqBatch batch) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5); t < batch.total_tiles;
+         t += nwarps) {
+        const GqDesc& D = batch.d[find_desc(batch, t)];
+        const int64_t b0 = (t - D.tile_begin) * kCopyTileBytes;
+        const int64_t nbytes_total = D.n_units * ES;
+        const int64_t left = nbytes_total - b0;
+        const int nbytes = left < kCopyTileBytes ? static_cast<int>(left) : kCopyTileBytes;
+        const uint8_t* src = D.src + b0;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(D.values) + b0;
+        if (D.perm_heads == 0) {
+            for (int c = lane * 16; c + 16 <= nbytes; c += 32 * 16)
+                stg128(dst + c, __ldg(reinterpret_cast<const uint4*>(src + c)));
+            for (int c = (nbytes & ~15) + lane * ES; c < nbytes; c += 32 * ES) {
+                if (ES == 4) *reinterpret_cast<uint32_t*>(dst + c) = *reinterpret_cast<const uint32_t*>(src + c);
+                else *reinterpret_cast<uint16_t*>(dst + c) = *reinterpret_cast<const uint16_t*>(src + c);
+            }
+        } else {
+            uint8_t* base = reinterpret_cast<uint8_t*>(D.values);
+            const int64_t e0 = b0 / ES;
+            for (int e = lane; e < nbytes / ES; e += 32) {
+                const int64_t oe = permute_unit(D, e0 + e);
+                if (ES == 4) reinterpret_cast<uint32_t*>(base)[oe] = reinterpret_cast<const uint32_t*>(src)[e];
+                else reinterpret_cast<uint16_t*>(base)[oe] = reinterpret_cast<const uint16_t*>(src)[e];
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// requantize_symmetric as a standalone scheme (ggml_quant.py:785-886): one thread per block
+// ---------------------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads) gq_requant_kernel(const float* __restrict__ bc,
+                                                              const int8_t* __restrict__ codes,
+                                                              int64_t n_blocks, int block, int bits,
+                                                              float* __restrict__ out_scales,
+                                                              int8_t* __restrict__ out_codes,
+                                                              gq_diag_t* diag) {
+    const int lane = threadIdx.x & 31;
+    const int lo_out = -(1 << (bits - 1));
+    const int hi_out = (1 << (bits - 1)) - 1;
+    DiagAcc acc;
+    acc.target = diag;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t start = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    // every lane walks the same number of iterations so the warp-collective flush stays uniform
+    const int64_t iters = (n_blocks + stride - 1) / stride;
+    for (int64_t it = 0; it < iters; ++it) {
+        const int64_t i = start + it * stride;
+        if (i >= n_blocks) continue;
+        const int8_t* q = codes + i * block;
+        int qmin = 127, qmax = -128;
+        for (int j = 0; j < block; ++j) {
+            qmin = min(qmin, static_cast<int>(q[j]));
+            qmax = max(qmax, static_cast<int>(q[j]));
+        }
+        const Requant p = requant_block(bc[2 * i], bc[2 * i + 1], qmin, qmax, lo_out, hi_out);
+        out_scales[i] = p.scale;
+        for (int j = 0; j < block; ++j)
+            out_codes[i * block + j] = static_cast<int8_t>(requant_value(q[j], p.sf, p.rm, lo_out, hi_out));
+        acc.add(p.round_err, p.clip_err);
+    }
+    acc.flush(lane);
+}
+
+// ---------------------------------------------------------------------------------------
+// Host-side launchers
+// ---------------------------------------------------------------------------------------
+
+namespace {
+
+struct DeviceInfo {
+    int sms = 0;
+};
+
+DeviceInfo& device_info() {
+    static DeviceInfo info[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    DeviceInfo& di = info[dev & 63];
+    if (di.sms == 0) cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev);
+    return di;
+}
+
+template <int TYPE, int MODE>
+int launch_fmt(const GqBatch& b, cudaStream_t s) {
+    using F = Fmt<TYPE>;
+    constexpr int smem = kWarps * F::kStages * F::kStageBytes;
+    static_assert(smem <= 48 * 1024, "stay within the default dynamic shared memory limit");
+    static int per_sm[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int& occ = per_sm[dev & 63];
+    if (occ == 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gq_convert_kernel<TYPE, MODE>, kThreads, smem) !=
+                cudaSuccess || occ < 1)
+            occ = 1;
+    }
+    const int64_t want = (b.total_tiles + kWarps - 1) / kWarps;
+    const int64_t cap = static_cast<int64_t>(device_info().sms) * occ;
+    const int blocks = static_cast<int>(want < cap ? want : cap);
+    if (blocks <= 0) return 0;
+    gq_convert_kernel<TYPE, MODE><<<blocks, kThreads, smem, s>>>(b);
+    return static_cast<int>(cudaGetLastError());
+}
+
+template <int TYPE>
+int launch_modes(int out_mask, const GqBatch& b, cudaStream_t s) {
+    switch (out_mask) {
+        case kOutCodes: return launch_fmt<TYPE, kOutCodes>(b, s);
+        case kOutF32: return launch_fmt<TYPE, kOutF32>(b, s);
+        default: return launch_fmt<TYPE, kOutCodes | kOutF32>(b, s);
+    }
+}
+
+template <int ES>
+int launch_copy(const GqBatch& b, cudaStream_t s) {
+    const int64_t want = (b.total_tiles + kWarps - 1) / kWarps;
+    const int64_t cap = static_cast<int64_t>(device_info().sms) * 8;
+    const int blocks = static_cast<int>(want < cap ? want : cap);
+    if (blocks <= 0) return 0;
+    gq_copy_kernel<ES><<<blocks, kThreads, 0, s>>>(b);
+    return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+int64_t tiles_for(int type, int64_t n_units) {
+    int upt;
+    switch (type) {
+        case GQ_TYPE_Q4_K: upt = Fmt<GQ_TYPE_Q4_K>::kUnitsPerTile; break;
+        case GQ_TYPE_Q5_K: upt = Fmt<GQ_TYPE_Q5_K>::kUnitsPerTile; break;
+        case GQ_TYPE_Q6_K: upt = Fmt<GQ_TYPE_Q6_K>::kUnitsPerTile; break;
+        case GQ_TYPE_Q8_0: upt = Fmt<GQ_TYPE_Q8_0>::kUnitsPerTile; break;
+        case GQ_TYPE_Q4_0: upt = Fmt<GQ_TYPE_Q4_0>::kUnitsPerTile; break;
+        case GQ_TYPE_F32: upt = kCopyTileBytes / 4; break;
+        default: upt = kCopyTileBytes / 2; break;   // F16, BF16
+    }
+    return (n_units + upt - 1) / upt;
+}
+
+int launch_batch(int type, int out_mask, const GqBatch& b, void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (type) {
+        case GQ_TYPE_Q4_K: return launch_modes<GQ_TYPE_Q4_K>(out_mask, b, s);
+        case GQ_TYPE_Q5_K: return launch_modes<GQ_TYPE_Q5_K>(out_mask, b, s);
+        case GQ_TYPE_Q6_K: return launch_modes<GQ_TYPE_Q6_K>(out_mask, b, s);
+        case GQ_TYPE_Q8_0: return launch_modes<GQ_TYPE_Q8_0>(out_mask, b, s);
+        case GQ_TYPE_Q4_0: return launch_modes<GQ_TYPE_Q4_0>(out_mask, b, s);
+        case GQ_TYPE_F32: return launch_copy<4>(b, s);
+        default: return launch_copy<2>(b, s);
+    }
+}
+
+int launch_requant(const float* bc, const int8_t* codes, int64_t n_blocks, int block, int bits,
+                   float* out_scales, int8_t* out_codes, gq_diag_t* diag, void* stream) {
+    const int64_t want = (n_blocks + kThreads - 1) / kThreads;
+    const int64_t cap = static_cast<int64_t>(device_info().sms) * 8;
+    const int blocks = static_cast<int>(want < cap ? want : cap);
+    if (blocks <= 0) return 0;
+    gq_requant_kernel<<<blocks, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        bc, codes, n_blocks, block, bits, out_scales, out_codes, diag);
+    return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace gq

@@ -1,0 +1,208 @@
+"""Drop-in GGUF tensor decode on B200: the call surface of ``sima_lmm.gguf.gguf_conversion``.
+
+``unpack_gguf_tensor(gguf_tensor, force_float)`` returns exactly what the reference
+function of the same name returns (``sima_lmm/gguf/gguf_conversion.py:102-176``): for
+quantized types ``(scales f32 (n_blocks, 1), codes (rows, cols))`` with int8 codes (or
+ml_dtypes int4 for Q4_0), for ``force_float=True`` ``(None, f32 (rows, cols))`` as
+gguf-py's ``dequantize`` computes it, and float tensors unchanged.  The decode runs in
+libgguf_b200.so through ``gq_convert_host``; there is no CPU fallback: a type outside
+the path (Q4_1, Q5_0, Q5_1, Q8_1, Q2_K, Q3_K, IQ*) raises ``NotImplementedError``.
+
+``GgufReaderProxy`` mirrors the reference class (``gguf_conversion.py:179-205``), and
+``install`` swaps this decode (and the fused q/k head permutation) into an imported
+reference module so that ``GgufModel`` and everything above it run unchanged.
+"""
+from __future__ import annotations
+
+import ctypes
+import logging
+import os
+import threading
+from pathlib import Path
+
+import numpy as np
+from ml_dtypes import bfloat16, int4
+
+from . import _native as N
+from .formats import FORMAT_BY_ID, FORMATS
+
+__all__ = ["unpack_gguf_tensor", "load_tensor", "convert_host", "GgufReaderProxy", "install",
+           "requant_warning"]
+
+# Same logger and text as ggml_quant.py:879-880, so log handling stays as it was.
+_log = logging.getLogger("sima_lmm.gguf.ggml_quant")
+
+_GPU_TYPES = {"Q8_0", "Q4_0", "Q4_K", "Q5_K", "Q6_K"}
+_sessions: dict[tuple[int, int], ctypes.c_void_p] = {}
+_sessions_lock = threading.Lock()
+
+
+def _device() -> int:
+    env = os.environ.get("LLIMA_B200_DEVICE")
+    if env is not None:
+        return int(env)
+    try:
+        import torch
+        if torch.cuda.is_available():
+            return torch.cuda.current_device()
+    except ImportError:
+        pass
+    return 0
+
+
+def _session(device: int) -> ctypes.c_void_p:
+    """Per-process, per-device session (created lazily, so spawned workers each get their
+    own CUDA context, as the reference's process pool needs)."""
+    key = (os.getpid(), device)
+    with _sessions_lock:
+        s = _sessions.get(key)
+        if s is None:
+            mb = int(os.environ.get("LLIMA_B200_STAGING_MB", "256"))
+            s = ctypes.c_void_p()
+            N.check(N.lib().gq_session_create(device, mb << 20, ctypes.byref(s)), "gq_session_create")
+            _sessions[key] = s
+    return s
+
+
+def requant_warning(round_error: np.float32, clip_error: np.int16) -> None:
+    """Log the reference's distortion warning when it would fire (ggml_quant.py:879-880)."""
+    if clip_error > 0 or round_error > 0.5:
+        _log.warning(f"Distortion from requantization: rounding {round_error}, clipping {clip_error}")
+
+
+def _host_ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def convert_host(fmt: str, raw: np.ndarray, rows: int, cols: int, force_float: bool = False,
+                 perm_heads: int = 0, device: int | None = None):
+    """GGUF bytes in host memory -> (scales | None, weights) in host memory, on the GPU.
+    Returns (scales, weights, (round_error, clip_error) | None)."""
+    f = FORMATS[fmt]
+    raw = np.ascontiguousarray(raw).reshape(-1).view(np.uint8)
+    n_values = rows * cols
+    if f.asymmetric and not force_float and n_values == 0:
+        # the reference's np.max over an empty requantization raises (ggml_quant.py:868)
+        raise ValueError("zero-size array to reduction operation maximum which has no identity")
+    rec = N.Tensor()
+    rec.type = f.type_id
+    rec.perm_heads = perm_heads
+    rec.rows = rows
+    rec.cols = cols
+    rec.src = _host_ptr(raw)
+    rec.src_bytes = raw.size
+    scales = codes = values = None
+    if force_float:
+        values = np.empty((rows, cols), dtype=np.float32)
+        rec.values = _host_ptr(values)
+        mask = N.OUT_F32
+    else:
+        codes = np.empty((rows, cols), dtype=np.int8)
+        scales = np.empty((n_values // f.block_values, 1), dtype=np.float32)
+        rec.codes = _host_ptr(codes)
+        rec.scales = _host_ptr(scales)
+        mask = N.OUT_CODES
+    diag = N.Diag()
+    dev = _device() if device is None else device
+    N.check(N.lib().gq_convert_host(_session(dev), ctypes.byref(rec), 1, mask, ctypes.byref(diag)),
+            "gq_convert_host")
+    if force_float:
+        return None, values, None
+    d = None
+    if f.asymmetric:
+        d = (np.array([diag.round_err_bits], dtype=np.uint32).view(np.float32)[0], np.int16(diag.clip_err))
+    if fmt == "Q4_0":
+        codes = codes.view(np.uint8).view(int4)
+    return scales, codes, d
+
+
+def _type_name(tensor_type) -> str:
+    tid = int(tensor_type)
+    f = FORMAT_BY_ID.get(tid)
+    if f is not None:
+        return f.name
+    return getattr(tensor_type, "name", str(tid))
+
+
+def load_tensor(gguf_tensor, force_float: bool, perm_heads: int = 0):
+    """``unpack_gguf_tensor`` plus the llama q/k head permutation fused into the decode
+    (``GgufModel.load_weight`` + ``_permute_qk_proj``, gguf_conversion.py:285-332)."""
+    name = _type_name(gguf_tensor.tensor_type)
+    shape = tuple(int(x) for x in gguf_tensor.shape[::-1])
+    if name in ("F32", "F16", "BF16"):
+        # float tensors are passed through unchanged (gguf_conversion.py:132-140)
+        if name == "F32":
+            w = np.asarray(gguf_tensor.data, dtype=np.float32)
+        elif name == "F16":
+            w = np.asarray(gguf_tensor.data, dtype=np.float16)
+        else:
+            w = np.frombuffer(gguf_tensor.data.tobytes(), dtype=bfloat16)
+        w = w.reshape(shape)
+        if perm_heads:
+            rows = shape[0]
+            w = w.reshape(perm_heads, rows // perm_heads // 2, 2, *shape[1:]).swapaxes(1, 2).reshape(shape)
+        return None, w
+    if name not in _GPU_TYPES:
+        raise NotImplementedError(f"GGML type {name} is not handled by the B200 GGUF path")
+    rows = shape[0]
+    cols = int(np.prod(shape[1:])) if len(shape) > 1 else 1
+    s, w, d = convert_host(name, np.asarray(gguf_tensor.data), rows, cols, force_float, perm_heads)
+    if d is not None:
+        requant_warning(*d)
+    return s, w.reshape(shape)
+
+
+def unpack_gguf_tensor(gguf_tensor, force_float: bool):
+    """Same inputs and outputs as ``sima_lmm.gguf.gguf_conversion.unpack_gguf_tensor``."""
+    return load_tensor(gguf_tensor, force_float, 0)
+
+
+class GgufReaderProxy:
+    """``GgufReaderProxy`` (gguf_conversion.py:179-205) with the B200 decode."""
+
+    def __init__(self, path: Path | str):
+        from gguf import GGUFReader
+        self._gguf_reader = GGUFReader(path)
+        self._tensor_map = {x.name: idx for idx, x in enumerate(self._gguf_reader.tensors)}
+
+    def load_tensor(self, tensor_name: str, force_float: bool, perm_heads: int = 0):
+        assert tensor_name in self._tensor_map, f"Tensor {tensor_name} not exist in tensor map."
+        gguf_tensor = self._gguf_reader.get_tensor(self._tensor_map[tensor_name])
+        return load_tensor(gguf_tensor, force_float, perm_heads)
+
+    def get_fields(self) -> dict:
+        return dict(self._gguf_reader.fields.items())
+
+    def get_tensor_info(self) -> dict:
+        info = {}
+        for name, idx in self._tensor_map.items():
+            t = self._gguf_reader.get_tensor(idx)
+            info[name] = {"gguf_type": t.tensor_type, "shape": tuple(t.shape[::-1])}
+        return info
+
+
+def install(module=None):
+    """Route an imported ``sima_lmm.gguf.gguf_conversion`` through the B200 path.
+
+    Replaces the module's ``unpack_gguf_tensor`` and ``GgufReaderProxy`` and makes
+    ``GgufModel.load_weight`` apply the llama q/k permutation inside the decode instead
+    of on the host afterwards.  Returns the module."""
+    if module is None:
+        import sima_lmm.gguf.gguf_conversion as module  # noqa: PLC0415 (reference package)
+    module.unpack_gguf_tensor = unpack_gguf_tensor
+    module.GgufReaderProxy = GgufReaderProxy
+    model_cls = module.GgufModel
+
+    def load_weight(self, name: str, is_hf_name: bool = True, force_float: bool = False):
+        if is_hf_name:
+            name = self.convert_hf_weight_name(name)
+        heads = 0
+        if self._need_permute_qk_proj:
+            if name.endswith(("attn_q.weight", "attn_q.bias")):
+                heads = self.model_config["num_attention_heads"]
+            elif name.endswith(("attn_k.weight", "attn_k.bias")):
+                heads = self.model_config["num_key_value_heads"]
+        return self.gguf_proxy.load_tensor(name, force_float, heads)
+
+    model_cls.load_weight = load_weight
+    return module

@@ -88,6 +88,43 @@ def gen_tensor_bytes(fmt: str, n_values: int, seed: int, kind: str = "weight") -
     return u.reshape(-1)
 
 
+def gen_tensor_bytes_torch(fmt: str, n_values: int, seed: int, device, kind: str = "weight"):
+    """Same distributions as ``gen_tensor_bytes``, generated with torch on `device` (the
+    byte streams differ from the numpy generator's).  Uniform bytes in the 12 packed
+    scale bytes of Q4_K/Q5_K are exactly uniform (scale, min) pairs, since the 6-bit
+    packing is a bijection between 16 six-bit values and 12 bytes."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    f = FORMATS[fmt]
+    if fmt == "F32":
+        mean = 1.0 if kind == "norm" else 0.0
+        x = torch.empty(n_values, dtype=torch.float32, device=device).normal_(mean, 0.02, generator=g)
+        return x.view(torch.uint8)
+    n = n_values // f.unit_values
+    u = torch.randint(0, 256, (n, f.unit_bytes), dtype=torch.uint8, device=device, generator=g)
+
+    def f16_field():
+        x = torch.empty(n, dtype=torch.float32, device=device).uniform_(1e-4, 1e-2, generator=g)
+        return x.to(torch.float16).view(torch.uint8).view(n, 2)
+
+    if fmt == "Q8_0":
+        u[:, 0:2] = f16_field()
+        u[:, 2:34] = torch.randint(-127, 128, (n, 32), dtype=torch.int8, device=device, generator=g).view(torch.uint8)
+    elif fmt == "Q4_0":
+        u[:, 0:2] = f16_field()
+    elif fmt in ("Q4_K", "Q5_K"):
+        u[:, 0:2] = f16_field()
+        u[:, 2:4] = f16_field()
+    elif fmt == "Q6_K":
+        u[:, 192:208] = ((u[:, 192:208] & 0x7F).to(torch.int16) - 64).to(torch.int8).view(torch.uint8)
+        u[:, 208:210] = f16_field()
+    else:
+        raise ValueError(f"unsupported synthetic format {fmt}")
+    return u.reshape(-1)
+
+
 @dataclass(frozen=True)
 class ModelShape:
     layers: int

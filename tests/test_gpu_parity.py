@@ -1,0 +1,272 @@
+"""Parity of the CUDA path (through the C ABI) with the reference.
+
+* every golden vector produced by the reference itself (tests/golden/);
+* the CPU oracle on seeded inputs at the BASELINE tensor shapes (config 1: Q8_0
+  4096x4096; config 2: Q4_0 and Q4_K 11008x4096; Q5_K and Q6_K alike);
+* the host-buffer path (gq_convert_host) against the device path;
+* the standalone requantization scheme against the oracle.
+
+Integer codes, f32 scales and f32 values are compared bit for bit (NaN == NaN).
+"""
+import ctypes
+
+import ml_dtypes
+import numpy as np
+import pytest
+import torch
+
+from llima_b200 import _native as N
+from llima_b200.device import DeviceTensor, alloc_outputs, convert, diag_values
+from llima_b200.formats import FORMATS
+from llima_b200.synth import gen_tensor_bytes
+from oracle import ggml_oracle as O
+from tests.golden_cases import case_names, load_case, same_bits
+
+pytestmark = pytest.mark.gpu
+BOTH = N.OUT_CODES | N.OUT_F32
+
+
+def _dev(raw: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(raw).copy()).cuda()
+
+
+def _codes_np(t: DeviceTensor) -> np.ndarray:
+    return t.codes.cpu().numpy()
+
+
+def _run(fmt, raw, rows, cols, mask=BOTH, heads=0):
+    t = DeviceTensor(fmt, rows, cols, _dev(raw), heads)
+    alloc_outputs(t, mask)
+    convert(t, mask)
+    torch.cuda.synchronize()
+    return t
+
+
+@pytest.mark.parametrize("case", case_names())
+def test_golden(case):
+    g = load_case(case)
+    fmt, rows, cols = g["fmt"], g["rows"], g["cols"]
+    heads = g.get("perm_heads", 0)
+    if FORMATS[fmt].block_values == 0:
+        t = _run(fmt, g["raw"], rows, cols, N.OUT_CODES, heads)
+        want = g["perm_codes"] if heads else g["codes"]
+        assert same_bits(t.values.cpu().numpy().reshape(want.shape), want)
+        return
+    t = _run(fmt, g["raw"], rows, cols, BOTH, heads)
+    codes = _codes_np(t)
+    want_codes = g["perm_codes"] if heads else g["codes"]
+    want_scales = g["perm_scales"] if heads else g["scales"]
+    assert same_bits(codes.view(np.uint8), want_codes.view(np.uint8)), case
+    assert same_bits(t.scales.cpu().numpy(), want_scales), case
+    if not heads:
+        assert same_bits(t.values.cpu().numpy(), g["f32"]), case
+    if FORMATS[fmt].asymmetric:
+        with np.errstate(all="ignore"):
+            _, _, d = O.unpack_tensor(fmt, g["raw"].tobytes(), (rows, cols), log=False)
+        r, c = diag_values(t.diag)
+        assert same_bits(np.float32(r), np.float32(d.round_error))
+        assert int(c) == int(d.clip_error)
+
+
+# BASELINE configs 1 and 2 at full size, plus the other two K formats at the same shape
+FULL = [("Q8_0", 4096, 4096), ("Q4_0", 11008, 4096), ("Q4_K", 11008, 4096),
+        ("Q5_K", 11008, 4096), ("Q6_K", 11008, 4096)]
+
+
+@pytest.mark.parametrize("fmt,rows,cols", FULL, ids=[f[0] for f in FULL])
+def test_full_size_vs_oracle(fmt, rows, cols):
+    raw = gen_tensor_bytes(fmt, rows * cols, 2024)
+    t = _run(fmt, raw, rows, cols, BOTH)
+    with np.errstate(all="ignore"):
+        s, w, d = O.unpack_tensor(fmt, raw.tobytes(), (rows, cols), log=False)
+        f32 = O.gguf_dequantize(raw.tobytes(), fmt).reshape(rows, cols)
+    wv = w.view(np.uint8) if w.dtype == ml_dtypes.int4 else w
+    assert same_bits(_codes_np(t).view(np.uint8), wv.view(np.uint8))
+    assert same_bits(t.scales.cpu().numpy(), s)
+    assert same_bits(t.values.cpu().numpy(), f32)
+    if d is not None:
+        r, c = diag_values(t.diag)
+        assert same_bits(np.float32(r), np.float32(d.round_error)) and int(c) == int(d.clip_error)
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0"])
+@pytest.mark.parametrize("mask", [N.OUT_CODES, N.OUT_F32])
+def test_single_output_modes_match_both(fmt, mask):
+    rows, cols = 64, 2048
+    raw = gen_tensor_bytes(fmt, rows * cols, 99)
+    both = _run(fmt, raw, rows, cols, BOTH)
+    one = _run(fmt, raw, rows, cols, mask)
+    if mask == N.OUT_CODES:
+        assert torch.equal(one.codes, both.codes) and torch.equal(one.scales.view(torch.int32),
+                                                                   both.scales.view(torch.int32))
+        assert one.values is None
+    else:
+        assert torch.equal(one.values.view(torch.int32), both.values.view(torch.int32))
+        assert one.codes is None
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K", "Q8_0"])
+def test_uniform_random_bytes_vs_oracle(fmt):
+    # every f16 field random: NaN, inf, subnormal and huge constants
+    f = FORMATS[fmt]
+    rows, cols = 128, 2048
+    n = rows * cols // f.unit_values
+    raw = np.frombuffer(np.random.default_rng(5).bytes(n * f.unit_bytes), dtype=np.uint8).copy()
+    t = _run(fmt, raw, rows, cols, BOTH)
+    with np.errstate(all="ignore"):
+        s, w, d = O.unpack_tensor(fmt, raw.tobytes(), (rows, cols), log=False)
+        f32 = O.gguf_dequantize(raw.tobytes(), fmt).reshape(rows, cols)
+    assert same_bits(_codes_np(t), w)
+    assert same_bits(t.scales.cpu().numpy(), s)
+    assert same_bits(t.values.cpu().numpy(), f32)
+
+
+def test_batch_matches_single_and_accumulates_diag():
+    from llima_b200.device import DeviceBatch
+    specs = [("Q4_K", 48, 1024, 0), ("Q6_K", 40, 512, 0), ("Q4_K", 64, 512, 4), ("Q5_K", 16, 256, 0),
+             ("Q8_0", 33, 64, 0), ("Q4_0", 7, 96, 0), ("F32", 64, 1, 4), ("Q6_K", 32, 256, 2)]
+    singles, batch = [], []
+    for i, (fmt, r, c, h) in enumerate(specs):
+        raw = gen_tensor_bytes(fmt, r * c, 300 + i, "bias")
+        singles.append(_run(fmt, raw, r, c, N.OUT_CODES, h))
+        batch.append(alloc_outputs(DeviceTensor(fmt, r, c, _dev(raw), h), N.OUT_CODES))
+    b = DeviceBatch(batch, N.OUT_CODES)
+    b.run()
+    torch.cuda.synchronize()
+    for s, t in zip(singles, batch):
+        for name in ("codes", "scales", "values"):
+            a, bb = getattr(s, name), getattr(t, name)
+            assert (a is None) == (bb is None)
+            if a is not None:
+                assert torch.equal(a.view(torch.uint8), bb.view(torch.uint8)), (t.fmt, name)
+    for i, (s, (fmt, *_)) in enumerate(zip(singles, specs)):
+        if FORMATS[fmt].asymmetric:
+            assert torch.equal(b.diags[i], s.diag)
+
+
+def test_permutation_matches_oracle_full_model_shapes():
+    # Llama-3-8B attn_q (32 heads) and attn_k (8 heads) at full size
+    for rows, heads in ((4096, 32), (1024, 8)):
+        raw = gen_tensor_bytes("Q4_K", rows * 4096, rows)
+        t = _run("Q4_K", raw, rows, 4096, N.OUT_CODES, heads)
+        with np.errstate(all="ignore"):
+            s, w, _ = O.unpack_tensor("Q4_K", raw.tobytes(), (rows, 4096), log=False)
+        ps, pw = O.permute_qk(s, w, heads)
+        assert same_bits(_codes_np(t), pw) and same_bits(t.scales.cpu().numpy(), ps)
+
+
+@pytest.mark.parametrize("fmt,rows,cols", [("Q4_K", 300, 4096), ("Q6_K", 257, 1024), ("Q8_0", 513, 4096),
+                                           ("F32", 4096, 1)])
+def test_host_path_matches_device(fmt, rows, cols):
+    from llima_b200.gguf_conversion import convert_host
+    raw = gen_tensor_bytes(fmt, rows * cols, 7, "norm")
+    if fmt == "F32":
+        return
+    t = _run(fmt, raw, rows, cols, BOTH)
+    s, w, d = convert_host(fmt, raw, rows, cols, False)
+    _, f, _ = convert_host(fmt, raw, rows, cols, True)
+    assert same_bits(w.view(np.uint8), _codes_np(t).view(np.uint8))
+    assert same_bits(s, t.scales.cpu().numpy())
+    assert same_bits(f, t.values.cpu().numpy())
+    if d is not None:
+        r, c = diag_values(t.diag)
+        assert same_bits(np.float32(d[0]), np.float32(r)) and int(d[1]) == int(c)
+
+
+def test_host_path_small_staging_splits_tensors(monkeypatch):
+    # a 1 MiB staging slot forces pieces: large tensors are split, small ones packed
+    from llima_b200 import gguf_conversion as G
+    monkeypatch.setenv("LLIMA_B200_STAGING_MB", "1")
+    monkeypatch.setattr(G, "_sessions", {})
+    raw = gen_tensor_bytes("Q4_K", 2048 * 4096, 8)
+    s, w, _ = G.convert_host("Q4_K", raw, 2048, 4096, False)
+    with np.errstate(all="ignore"):
+        s2, w2, _ = O.unpack_tensor("Q4_K", raw.tobytes(), (2048, 4096), log=False)
+    assert same_bits(w, w2) and same_bits(s, s2)
+
+
+def test_unpack_gguf_tensor_dropin_reader(tmp_path):
+    gguf = pytest.importorskip("gguf")
+    from llima_b200.gguf_conversion import GgufReaderProxy
+    path = tmp_path / "t.gguf"
+    w = gguf.GGUFWriter(str(path), "llama")
+    tensors = {}
+    for i, (fmt, r, c) in enumerate([("Q4_K", 8, 512), ("Q6_K", 4, 256), ("Q8_0", 6, 64), ("Q4_0", 3, 32)]):
+        raw = gen_tensor_bytes(fmt, r * c, 40 + i)
+        name = f"blk.0.t{i}.weight"
+        w.add_tensor(name, raw.reshape(r, -1), raw_shape=(r, raw.size // r),
+                     raw_dtype=getattr(gguf.GGMLQuantizationType, fmt))
+        tensors[name] = (fmt, raw, r, c)
+    norm = np.random.default_rng(1).normal(1, 0.02, 64).astype(np.float32)
+    w.add_tensor("blk.0.attn_norm.weight", norm)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    proxy = GgufReaderProxy(path)
+    for name, (fmt, raw, r, c) in tensors.items():
+        s, q = proxy.load_tensor(name, False)
+        with np.errstate(all="ignore"):
+            s2, q2, _ = O.unpack_tensor(fmt, raw.tobytes(), (r, c), log=False)
+        assert q.dtype == q2.dtype and q.shape == (r, c)
+        assert same_bits(q.view(np.uint8), q2.view(np.uint8)) and same_bits(s, s2)
+        _, f = proxy.load_tensor(name, True)
+        assert same_bits(f, O.gguf_dequantize(raw.tobytes(), fmt).reshape(r, c))
+    s, n = proxy.load_tensor("blk.0.attn_norm.weight", False)
+    assert s is None and np.array_equal(n, norm)
+
+
+def test_requantize_symmetric_scheme_vs_oracle():
+    rng = np.random.default_rng(11)
+    n, block = 5000, 32
+    bc = np.stack([rng.uniform(-1e-2, 1e-2, n), -rng.uniform(0, 0.3, n)], 1).astype(np.float32)
+    bc[::17, 0] = 0
+    bc[::23, 1] = 0
+    q = rng.integers(0, 32, size=(n, block), dtype=np.int8)
+    dq, dbc = torch.from_numpy(q).cuda(), torch.from_numpy(bc).cuda()
+    out_s = torch.empty(n, dtype=torch.float32, device="cuda")
+    out_q = torch.empty((n, block), dtype=torch.int8, device="cuda")
+    diag = torch.zeros(2, dtype=torch.int32, device="cuda")
+    N.check(N.lib().gq_requantize_symmetric(dbc.data_ptr(), dq.data_ptr(), n, block, 8, out_s.data_ptr(),
+                                            out_q.data_ptr(), diag.data_ptr(), None), "requant")
+    torch.cuda.synchronize()
+    with np.errstate(all="ignore"):
+        s, q2, d = O.requantize_symmetric(bc, q, 8, np.int8, log=False)
+    assert same_bits(out_s.cpu().numpy().reshape(-1, 1), s)
+    assert same_bits(out_q.cpu().numpy(), q2)
+    r, c = diag_values(diag)
+    assert same_bits(np.float32(r), np.float32(d.round_error)) and int(c) == int(d.clip_error)
+
+
+def test_invalid_arguments_return_errors_without_launch():
+    lib = N.lib()
+    buf = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    t = N.Tensor()
+    t.type, t.rows, t.cols = 12, 1, 256
+    t.src, t.src_bytes = buf.data_ptr() + 1, 144   # misaligned source
+    t.codes, t.scales = buf.data_ptr() + 1024, buf.data_ptr() + 2048
+    assert lib.gq_convert(ctypes.byref(t), N.OUT_CODES, None) == -3
+    t.src = buf.data_ptr()
+    t.src_bytes = 100                               # too short
+    assert lib.gq_convert(ctypes.byref(t), N.OUT_CODES, None) == -2
+    t.src_bytes = 144
+    t.scales = None                                 # missing output
+    assert lib.gq_convert(ctypes.byref(t), N.OUT_CODES, None) == -4
+    t.scales = buf.data_ptr() + 2048
+    assert lib.gq_convert(ctypes.byref(t), 7, None) == -5
+    t.perm_heads = 3                                # rows not divisible by 2*heads
+    assert lib.gq_convert(ctypes.byref(t), N.OUT_CODES, None) == -5
+    t.perm_heads = 0
+    t.type = 3                                      # Q4_1: not on this path
+    assert lib.gq_convert(ctypes.byref(t), N.OUT_CODES, None) == -1
+    t.type, t.rows = 12, 0                          # empty tensor: nothing to do
+    assert lib.gq_convert(ctypes.byref(t), N.OUT_CODES, None) == 0
+    torch.cuda.synchronize()
+
+
+def test_empty_asymmetric_tensor_raises_like_reference():
+    from llima_b200.gguf_conversion import convert_host
+    with pytest.raises(ValueError, match="zero-size array"):
+        convert_host("Q4_K", np.zeros(0, dtype=np.uint8), 0, 256)
+    s, w, _ = convert_host("Q6_K", np.zeros(0, dtype=np.uint8), 0, 256)
+    assert s.shape == (0, 1) and w.shape == (0, 256)
