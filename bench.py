@@ -47,7 +47,27 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="keep only the first L transformer layers (small cases for profiling)")
+    ap.add_argument("--formats", default="", help="comma list of GGML formats to keep (profiling)")
     return ap.parse_args()
+
+
+def selected_specs(args):
+    """The model's tensor list, optionally cut to the first --layers layers / --formats."""
+    from llima_b200.synth import model_specs
+    specs = model_specs(args.model, args.seed)
+    if args.layers:
+        keep = []
+        for s in specs:
+            if s.name.startswith("blk."):
+                if int(s.name.split(".")[1]) < args.layers:
+                    keep.append(s)
+        specs = keep
+    if args.formats:
+        fm = set(args.formats.split(","))
+        specs = [s for s in specs if s.fmt in fm]
+    return specs
 
 
 # ---------------------------------------------------------------------------------------
@@ -189,8 +209,7 @@ def traffic_per_byte(kernel: str):
 
 def workload_config(args, world) -> dict:
     from llima_b200.formats import output_layout
-    from llima_b200.synth import model_specs
-    specs = model_specs(args.model, args.seed)
+    specs = selected_specs(args)
     gguf = sum(s.nbytes for s in specs)
     out = 0
     for s in specs:
@@ -200,7 +219,10 @@ def workload_config(args, world) -> dict:
         else:
             out += (lay["codes"] + lay["scales"] if args.out in ("codes", "both") else 0) + \
                 (lay["values"] if args.out in ("f32", "both") else 0)
-    return {"workload": f"{args.model} GGUF tensor set, whole model per step", "model": args.model,
+    cut = ""
+    if args.layers or args.formats:
+        cut = f" (cut: layers={args.layers or 'all'}, formats={args.formats or 'all'})"
+    return {"workload": f"{args.model} GGUF tensor set, whole model per step{cut}", "model": args.model,
             "n_tensors": len(specs), "gguf_bytes": gguf, "out_bytes": out, "output": args.out,
             "parallelism": f"tensor-shard x{world}",
             "l2": "inputs larger than L2 (GGUF bytes >> 126 MB), no flush"}
@@ -214,14 +236,14 @@ def run_ours(args, rank, world, local_rank):
     from llima_b200.device import DeviceBatch, DeviceTensor, alloc_outputs
     from llima_b200.formats import FORMATS
     from llima_b200.shard import piece_cost, plan_shards
-    from llima_b200.synth import gen_tensor_bytes_torch, head_count_for, model_specs
+    from llima_b200.synth import gen_tensor_bytes_torch, head_count_for
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     out_mask = {"codes": N.OUT_CODES, "f32": N.OUT_F32, "both": N.OUT_CODES | N.OUT_F32}[args.out]
     N.lib()   # fail loudly before any work if the library is missing
 
-    specs = model_specs(args.model, args.seed)
+    specs = selected_specs(args)
     plan = plan_shards([(s.fmt, s.rows, s.cols, head_count_for(args.model, s.name) > 0) for s in specs],
                        world, args.out)
     mine = plan[rank]

@@ -47,34 +47,48 @@ struct Requant {
 
 // ggml_quant.py:826-882 for one block with scale S, min M (already the negated f16
 // min), and the block's smallest / largest unsigned code.  Output range [lo_out, hi_out].
+//
+// Bound used below: for finite r, |r * sf| < 2200 (if r >= 0, sf <= 127/(qmax + r) or
+// r <= 7.94; if r < 0, sf <= 128/(|r| - qmin) or |r| <= qmin + 8, with int8 codes), and
+// for infinite or NaN r the product is NaN.  So numpy's int16(int32(rint(r*sf))) equals
+// cvt.rni (round half even, NaN -> 0) here, and no int16 sum can wrap.
 __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int qmax,
                                                  int lo_out, int hi_out) {
     Requant p;
     const float s_eff = (S == 0.0f) ? ((fabsf(M) > kScaleEpsilon) ? M : kScaleEpsilon) : S;
     const float r = __fdiv_rn(M, s_eff);
-    const float lo = __fadd_rn(static_cast<float>(qmin), r);
-    const float hi = __fadd_rn(static_cast<float>(qmax), r);
+    const float qminf = static_cast<float>(qmin);
+    const float qmaxf = static_cast<float>(qmax);
+    const float lo = __fadd_rn(qminf, r);
+    const float hi = __fadd_rn(qmaxf, r);
     float sf = 16.0f;
     // np.minimum(16, -128/lo) and np.minimum(sf, 127/hi).  Neither quotient can be NaN
     // here (lo < 0 and hi > 0 exclude NaN), so fminf matches np.minimum.  A quotient of
     // 16 or more cannot lower sf, so the division is skipped exactly then.
     if (lo < static_cast<float>(lo_out) / 16.0f) sf = fminf(sf, __fdiv_rn(static_cast<float>(lo_out), lo));
     if (hi > static_cast<float>(hi_out) / 16.0f) sf = fminf(sf, __fdiv_rn(static_cast<float>(hi_out), hi));
-    if (sf > 0.98f) sf = fmaxf(floorf(sf), 1.0f);
+    const bool big = sf > 0.98f;
+    if (big) sf = fmaxf(floorf(sf), 1.0f);
     const float rmv = __fmul_rn(r, sf);
-    const int rm = f32_to_i16_x86(rintf(rmv));
+    const int rm = __float2int_rn(rmv);
     p.sf = sf;
     p.rm = rm;
-    p.round_err = fabsf(__fsub_rn(static_cast<float>(rm), rmv));
+    p.round_err = fabsf(__fsub_rn(rintf(rmv), rmv));
     p.scale = __fdiv_rn(S, sf);
-    // q' is monotone in q (sf >= 0, |rm| < 2^10, no int16 wrap), so the block's extreme
-    // codes bound the clipping of every code.
-    const int vmin = f32_to_i16_x86(rintf(__fmul_rn(static_cast<float>(qmin), sf))) + rm;
-    const int vmax = f32_to_i16_x86(rintf(__fmul_rn(static_cast<float>(qmax), sf))) + rm;
+    p.fast = big || (sf == 0.0f);
+    int vmin, vmax;
+    if (p.fast) {
+        p.sfi = static_cast<int>(sf);
+        vmin = qmin * p.sfi + rm;
+        vmax = qmax * p.sfi + rm;
+    } else {
+        p.sfi = 0;
+        vmin = __float2int_rn(__fmul_rn(qminf, sf)) + rm;
+        vmax = __float2int_rn(__fmul_rn(qmaxf, sf)) + rm;
+    }
+    // q' is monotone in q (sf >= 0), so the block's extreme codes bound every code's clipping.
     p.clip = (vmax > hi_out) || (vmin < lo_out);
     p.clip_err = max(0, max(vmax - hi_out, lo_out - vmin));
-    p.fast = (sf > 0.98f) || (sf == 0.0f);
-    p.sfi = p.fast ? static_cast<int>(sf) : 0;
     return p;
 }
 
@@ -112,6 +126,26 @@ __device__ __forceinline__ uint32_t requant_word_slow(uint32_t x, float sf, int 
         out |= (static_cast<uint32_t>(requant_value(q, sf, rm, lo_out, hi_out)) & 0xFFu) << (8 * b);
     }
     return out;
+}
+
+// 16-bit-lane SIMD min / max (native on sm_90+) and multiply-high-add
+__device__ __forceinline__ uint32_t vmin16(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("min.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t vmax16(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t vmin16(uint32_t a, uint32_t b, uint32_t c) { return vmin16(vmin16(a, b), c); }
+__device__ __forceinline__ uint32_t vmax16(uint32_t a, uint32_t b, uint32_t c) { return vmax16(vmax16(a, b), c); }
+// high 32 bits of a*b, plus c
+__device__ __forceinline__ uint32_t mad_hi(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
 }
 
 // min / max of the 4 bytes of a word

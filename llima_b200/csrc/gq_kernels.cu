@@ -41,8 +41,8 @@ struct Fmt;
         static_assert(kTileBytes % 16 == 0, "tiles must be whole 16-byte chunks");        \
     };
 
-GQ_FMT(GQ_TYPE_Q4_K, 144, 4, 4)   // 32 blocks of 32 per tile
-GQ_FMT(GQ_TYPE_Q5_K, 176, 4, 4)
+GQ_FMT(GQ_TYPE_Q4_K, 144, 8, 4)   // 64 blocks of 32 per tile: one 32-byte group per lane
+GQ_FMT(GQ_TYPE_Q5_K, 176, 8, 4)
 GQ_FMT(GQ_TYPE_Q6_K, 210, 8, 3)   // 128 blocks of 16 per tile
 GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4)   // 32 blocks of 32 per tile
 GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4)
@@ -62,11 +62,22 @@ __device__ __forceinline__ int find_desc(const GqBatch& b, int64_t t) {
     return lo;
 }
 
+// A warp visits its tiles in increasing order, so the owning tensor only moves forward:
+// a cursor that steps ahead replaces a search per tile.
+struct DescCursor {
+    int idx = 0;
+    __device__ __forceinline__ int seek(const GqBatch& b, int64_t t) {
+        while (idx + 1 < b.n && b.d[idx + 1].tile_begin <= t) ++idx;
+        return idx;
+    }
+};
+
 // Enqueue the cp.async copies of tile `t` into `stage` (nothing when t is past the end).
 template <class F>
-__device__ __forceinline__ void issue_tile(const GqBatch& b, int64_t t, uint8_t* stage, int lane) {
+__device__ __forceinline__ void issue_tile(const GqBatch& b, DescCursor& cur, int64_t t, uint8_t* stage,
+                                           int lane) {
     if (t >= b.total_tiles) return;
-    const GqDesc& d = b.d[find_desc(b, t)];
+    const GqDesc& d = b.d[cur.seek(b, t)];
     const int64_t unit0 = (t - d.tile_begin) * F::kUnitsPerTile;
     const int64_t left = d.n_units - unit0;
     const int nunits = left < F::kUnitsPerTile ? static_cast<int>(left) : F::kUnitsPerTile;
@@ -82,136 +93,225 @@ __device__ __forceinline__ void issue_tile(const GqBatch& b, int64_t t, uint8_t*
 // Q4_K / Q5_K: 256-value super-blocks -> 8 blocks of 32, asymmetric -> symmetric int8
 //   Q4_K: d, dmin | scales[12] | qs[128]          (ggml_quant.py:624-642)
 //   Q5_K: d, dmin | scales[12] | qh[32] | qs[128]  (ggml_quant.py:643-661)
+//
+// A tile is 8 super-blocks = 32 groups of 32 nibble bytes; lane l owns group l
+// (super-block l/4, group g = l%4), i.e. block 2g (low nibbles) and block 2g+1 (high
+// nibbles).  Codes are kept in 16-bit lanes without shifting them down: for a word of
+// four bytes b0..b3,
+//   EL = w & 0x000F000F   low nibbles of b0, b2  (value << 0)
+//   OL = w & 0x0F000F00   low nibbles of b1, b3  (value << 8)
+//   EH = w & 0x00F000F0   high nibbles of b0, b2 (value << 4)
+//   OH = w & 0xF000F000   high nibbles of b1, b3 (value << 12; Q5_K: shifted down)
+// so the same masked words feed the min/max scan and the requantization: q*sf + rm is
+// one IMAD per two codes (mad.hi undoes the << 8 / << 12 for free).
 // ---------------------------------------------------------------------------------------
 
-template <bool Q5, int MODE>
-__device__ __forceinline__ void process_q45k(const GqDesc& D, int64_t unit0, int nunits,
-                                             const uint8_t* tile, int lane, DiagAcc& acc) {
+// Codes of one block side from its two 16-bit-lane words (E holds bytes 0 and 2, O bytes
+// 1 and 3, both already at bits 0..4 of their lanes) as a word of four code bytes.
+__device__ __forceinline__ uint32_t codes_word(uint32_t e, uint32_t o) { return __byte_perm(e, o, 0x6240); }
+
+// Requantized bytes of one word, slow path (non-integer scale factor) or with clipping.
+__device__ __forceinline__ uint32_t requant_word_general(uint32_t q4, const Requant& p) {
+    if (p.fast) {
+        uint32_t out = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int v = min(max(static_cast<int>((q4 >> (8 * b)) & 0xFF) * p.sfi + p.rm, -128), 127);
+            out |= (static_cast<uint32_t>(v) & 0xFFu) << (8 * b);
+        }
+        return out;
+    }
+    return requant_word_slow(q4, p.sf, p.rm, -128, 127);
+}
+
+template <bool Q5, int MODE, bool SECTOR_PAIRS>
+__device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int nunits,
+                                            const uint8_t* tile, int lane, DiagAcc& acc) {
     constexpr int UB = Q5 ? 176 : 144;
     constexpr int QS = Q5 ? 48 : 16;   // offset of the nibble bytes
-    constexpr int QH = 16;             // offset of the fifth-bit bytes (Q5_K)
-
-    // ---- parameter step: lane = block (super-block lane/8, sub-block lane%8)
-    const int sb = lane >> 3;
-    const int k = lane & 7;
+    const int sb = lane >> 2;
+    const int g = lane & 3;
     const bool valid = sb < nunits;
     const uint8_t* sbp = tile + sb * UB;
 
+    // ---- 6-bit scale / min of blocks 2g and 2g+1 (ggml_quant.py:352-375): byte j of the
+    // first / second / third word of the 12 scale bytes, for j = (2g)&3 and (2g)&3 + 1
     const uint32_t hdr = lds32(sbp);
-    const uint32_t s0 = lds32(sbp + 4), s1 = lds32(sbp + 8), s2 = lds32(sbp + 12);
-    int sc, mn;   // 6-bit scale / min of sub-block k (ggml_quant.py:352-375)
-    if (k < 4) {
-        sc = byte_of(s0, k) & 63;
-        mn = byte_of(s1, k) & 63;
-    } else {
-        const int j = k - 4;
-        sc = (byte_of(s2, j) & 15) | ((byte_of(s0, j) >> 6) << 4);
-        mn = (byte_of(s2, j) >> 4) | ((byte_of(s1, j) >> 6) << 4);
-    }
+    const uint32_t sel = (g & 1) ? 0x4432u : 0x4410u;
+    const uint32_t b0 = __byte_perm(lds32(sbp + 4), 0, sel);
+    const uint32_t b1 = __byte_perm(lds32(sbp + 8), 0, sel);
+    const uint32_t b2 = __byte_perm(lds32(sbp + 12), 0, sel);
+    const uint32_t sc2 = (g < 2) ? (b0 & 0x3F3Fu) : ((b2 & 0x0F0Fu) | ((b0 >> 2) & 0x3030u));
+    const uint32_t mn2 = (g < 2) ? (b1 & 0x3F3Fu) : (((b2 >> 4) & 0x0F0Fu) | ((b1 >> 2) & 0x3030u));
     const float d = h2f(hdr);
     const float dmin = h2f(hdr >> 16);
+    const int scL = sc2 & 0xFF, scH = sc2 >> 8, mnL = mn2 & 0xFF, mnH = mn2 >> 8;
 
-    Requant p{};
-    if (MODE & kOutCodes) {
-        const uint8_t* qs = sbp + QS + 32 * (k >> 1);
-        const uint4 a = lds128(qs), b = lds128(qs + 16);
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        uint32_t h[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (Q5) {
-            const uint4 ha = lds128(sbp + QH), hb = lds128(sbp + QH + 16);
-            h[0] = ha.x; h[1] = ha.y; h[2] = ha.z; h[3] = ha.w;
-            h[4] = hb.x; h[5] = hb.y; h[6] = hb.z; h[7] = hb.w;
-        }
-        const int shift = 4 * (k & 1);
-        uint32_t mn4 = 0xFFFFFFFFu, mx4 = 0u;
+    // ---- the group's 32 code bytes in the four lane layouts
+    const uint8_t* qp = sbp + QS + 32 * g;
+    const uint4 qa = lds128(qp), qb = lds128(qp + 16);
+    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    uint32_t EL[8], OL[8], EH[8], OH[8];
+    if (!Q5) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            uint32_t x = (w[i] >> shift) & 0x0F0F0F0Fu;
-            if (Q5) x |= ((h[i] >> k) & 0x01010101u) << 4;
-            mn4 = __vminu4(mn4, x);
-            mx4 = __vmaxu4(mx4, x);
+            EL[i] = w[i] & 0x000F000Fu;
+            OL[i] = w[i] & 0x0F000F00u;
+            EH[i] = w[i] & 0x00F000F0u;
+            OH[i] = w[i] & 0xF000F000u;
         }
-        // block constants: f16(f32 product), min negated (ggml_quant.py:771-777)
-        const float S = round_to_f16(__fmul_rn(static_cast<float>(sc), d));
-        const float M = -round_to_f16(__fmul_rn(static_cast<float>(mn), dmin));
-        p = requant_block(S, M, byte_min4(mn4), byte_max4(mx4), -128, 127);
-        if (valid) {
-            const int64_t ou = permute_unit(D, unit0 + sb);
-            D.scales[ou * 8 + k] = p.scale;
-            acc.add(p.round_err, p.clip_err);
+    } else {
+        // fifth bit of block k is bit k of qh[j] (ggml_quant.py:311-349): bit 2g for the
+        // low nibbles, 2g+1 for the high nibbles
+        const uint4 ha = lds128(sbp + 16), hb = lds128(sbp + 32);
+        const uint32_t h[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t t = h[i] >> (2 * g);
+            const uint32_t t4 = t << 4;
+            EL[i] = (w[i] & 0x000F000Fu) | (t4 & 0x00100010u);
+            OL[i] = (w[i] & 0x0F000F00u) | (t4 & 0x10001000u);
+            EH[i] = (w[i] & 0x00F000F0u) | ((t << 7) & 0x01000100u);
+            OH[i] = ((w[i] >> 12) & 0x000F000Fu) | ((t >> 5) & 0x00100010u);
         }
     }
-    // gguf-py dequantize: (d*sc)*q - dmin*m, each product rounded (Q4_K/Q5_K.dequantize_blocks)
-    const float dsc = __fmul_rn(d, static_cast<float>(sc));
-    const float dm = __fmul_rn(dmin, static_cast<float>(mn));
+    constexpr int kOHShift = Q5 ? 0 : 12;
 
-    // ---- apply step: lane = 16 codes (chunk c of the tile: block c/2, half c%2)
+    Requant pL{}, pH{};
+    if (MODE & kOutCodes) {
+        // ---- block min / max of the codes (16-bit-lane SIMD)
+        uint32_t mnEL = vmin16(EL[0], EL[1], EL[2]), mxEL = vmax16(EL[0], EL[1], EL[2]);
+        uint32_t mnOL = vmin16(OL[0], OL[1], OL[2]), mxOL = vmax16(OL[0], OL[1], OL[2]);
+        uint32_t mnEH = vmin16(EH[0], EH[1], EH[2]), mxEH = vmax16(EH[0], EH[1], EH[2]);
+        uint32_t mnOH = vmin16(OH[0], OH[1], OH[2]), mxOH = vmax16(OH[0], OH[1], OH[2]);
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const int c = 32 * r + lane;
-        const int src_lane = c >> 1;
-        float sf = 0.f;
-        int rm = 0, flags = 0;
-        if (MODE & kOutCodes) {
-            sf = __shfl_sync(kFull, p.sf, src_lane);
-            rm = __shfl_sync(kFull, p.rm, src_lane);
-            flags = __shfl_sync(kFull, (p.fast ? 1 : 0) | (p.clip ? 2 : 0) | (p.sfi << 2), src_lane);
+        for (int i = 3; i < 8; i += 2) {
+            const int j = i + 1 < 8 ? i + 1 : i;
+            mnEL = vmin16(mnEL, EL[i], EL[j]);
+            mxEL = vmax16(mxEL, EL[i], EL[j]);
+            mnOL = vmin16(mnOL, OL[i], OL[j]);
+            mxOL = vmax16(mxOL, OL[i], OL[j]);
+            mnEH = vmin16(mnEH, EH[i], EH[j]);
+            mxEH = vmax16(mxEH, EH[i], EH[j]);
+            mnOH = vmin16(mnOH, OH[i], OH[j]);
+            mxOH = vmax16(mxOH, OH[i], OH[j]);
         }
-        float cdsc = 0.f, cdm = 0.f;
-        if (MODE & kOutF32) {
-            cdsc = __shfl_sync(kFull, dsc, src_lane);
-            cdm = __shfl_sync(kFull, dm, src_lane);
+        const uint32_t aminL = vmin16(mnEL, mnOL >> 8), amaxL = vmax16(mxEL, mxOL >> 8);
+        const uint32_t aminH = vmin16(mnEH >> 4, mnOH >> kOHShift), amaxH = vmax16(mxEH >> 4, mxOH >> kOHShift);
+        const int qminL = min(aminL & 0xFFFF, aminL >> 16), qmaxL = max(amaxL & 0xFFFF, amaxL >> 16);
+        const int qminH = min(aminH & 0xFFFF, aminH >> 16), qmaxH = max(amaxH & 0xFFFF, amaxH >> 16);
+
+        // ---- block constants f16(f32 product), min negated (ggml_quant.py:771-777), then
+        // requantize_symmetric (ggml_quant.py:785-886)
+        const float SL = round_to_f16(__fmul_rn(static_cast<float>(scL), d));
+        const float SH = round_to_f16(__fmul_rn(static_cast<float>(scH), d));
+        const float ML = -round_to_f16(__fmul_rn(static_cast<float>(mnL), dmin));
+        const float MH = -round_to_f16(__fmul_rn(static_cast<float>(mnH), dmin));
+        pL = requant_block(SL, ML, qminL, qmaxL, -128, 127);
+        pH = requant_block(SH, MH, qminH, qmaxH, -128, 127);
+    }
+
+    const int64_t ou = permute_unit(D, unit0 + sb);
+    const int64_t off = ou * 256 + 64 * g;   // codes / values of block 2g, then 2g+1
+
+    if (MODE & kOutCodes) {
+        if (valid) {
+            *reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g) = make_float2(pL.scale, pH.scale);
+            acc.add(pL.round_err, pL.clip_err);
+            acc.add(pH.round_err, pH.clip_err);
         }
-        const int csb = c >> 4;
-        if (csb >= nunits) continue;
-        const int ck = (c >> 1) & 7;
-        const int ch = c & 1;
-        const uint8_t* base = tile + csb * UB;
-        const uint4 xv = lds128(base + QS + 32 * (ck >> 1) + 16 * ch);
-        uint32_t x[4] = {xv.x, xv.y, xv.z, xv.w};
-        const int shift = 4 * (ck & 1);
-        if (Q5) {
-            const uint4 hv = lds128(base + QH + 16 * ch);
-            const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+        uint32_t lo[8], hi[8];
+        constexpr uint32_t kBias = 0x400u;   // lane value q*sf + rm + bias stays in [0, 4096)
+        constexpr uint32_t kLo2 = (kBias - 128u) * 0x00010001u, kHi2 = (kBias + 127u) * 0x00010001u;
+        const uint32_t sfiL = static_cast<uint32_t>(pL.sfi), sfiH = static_cast<uint32_t>(pH.sfi);
+        const uint32_t KL = static_cast<uint32_t>(pL.rm + static_cast<int>(kBias)) * 0x00010001u;
+        const uint32_t KH = static_cast<uint32_t>(pH.rm + static_cast<int>(kBias)) * 0x00010001u;
+        const bool plainL = pL.fast && !pL.clip, plainH = pH.fast && !pH.clip;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                x[i] = ((x[i] >> shift) & 0x0F0F0F0Fu) | (((hw[i] >> ck) & 0x01010101u) << 4);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) x[i] = (x[i] >> shift) & 0x0F0F0F0Fu;
+        for (int i = 0; i < 8; ++i) {
+            // low nibbles: EL * sf + K and high32(OL * (sf << 24)) + K; high nibbles:
+            // (EH * sf + 16K) >> 4 and high32(OH * (sf << 20)) + K (Q5_K: OH * sf + K)
+            lo[i] = codes_word(EL[i] * sfiL + KL, mad_hi(OL[i], sfiL << 24, KL));
+            const uint32_t eh = (EH[i] * sfiH + (KH << 4)) >> 4;
+            const uint32_t oh = Q5 ? OH[i] * sfiH + KH : mad_hi(OH[i], sfiH << 20, KH);
+            hi[i] = codes_word(eh, oh);
         }
-        const int64_t ou = permute_unit(D, unit0 + csb);
-        const int64_t off = ou * 256 + 16 * (c & 15);
-        if (MODE & kOutCodes) {
-            uint4 o;
-            if (flags & 1) {
-                const uint32_t sfi = static_cast<uint32_t>(flags >> 2);
-                const uint32_t k2 = static_cast<uint32_t>(rm + static_cast<int>(kLaneBias)) * 0x00010001u;
-                const bool clip = (flags & 2) != 0;
-                constexpr uint32_t lo2 = (kLaneBias - 128u) * 0x00010001u;
-                constexpr uint32_t hi2 = (kLaneBias + 127u) * 0x00010001u;
-                o.x = requant_word_fast(x[0], sfi, k2, clip, lo2, hi2);
-                o.y = requant_word_fast(x[1], sfi, k2, clip, lo2, hi2);
-                o.z = requant_word_fast(x[2], sfi, k2, clip, lo2, hi2);
-                o.w = requant_word_fast(x[3], sfi, k2, clip, lo2, hi2);
-            } else {
-                o.x = requant_word_slow(x[0], sf, rm, -128, 127);
-                o.y = requant_word_slow(x[1], sf, rm, -128, 127);
-                o.z = requant_word_slow(x[2], sf, rm, -128, 127);
-                o.w = requant_word_slow(x[3], sf, rm, -128, 127);
+        if (!plainL) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (pL.fast) {
+                    const uint32_t e = vmin16(vmax16(EL[i] * sfiL + KL, kLo2), kHi2);
+                    const uint32_t o = vmin16(vmax16(mad_hi(OL[i], sfiL << 24, KL), kLo2), kHi2);
+                    lo[i] = codes_word(e, o);
+                } else {
+                    lo[i] = requant_word_general(codes_word(EL[i], OL[i] >> 8), pL);
+                }
             }
-            stg128(D.codes + off, o);
         }
-        if (MODE & kOutF32) {
-            float* dst = D.values + off;
+        if (!plainH) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (pH.fast) {
+                    const uint32_t e = vmin16(vmax16((EH[i] * sfiH + (KH << 4)) >> 4, kLo2), kHi2);
+                    const uint32_t oh = Q5 ? OH[i] * sfiH + KH : mad_hi(OH[i], sfiH << 20, KH);
+                    const uint32_t o = vmin16(vmax16(oh, kLo2), kHi2);
+                    hi[i] = codes_word(e, o);
+                } else {
+                    hi[i] = requant_word_general(codes_word(EH[i] >> 4, OH[i] >> kOHShift), pH);
+                }
+            }
+        }
+        // 64 output bytes per lane as four 16-byte chunks c0..c3 (c0,c1: block 2g; c2,c3:
+        // block 2g+1).  With SECTOR_PAIRS, lanes 2m and 2m+1 (adjacent 64-byte regions of
+        // one super-block) swap chunks so that every store instruction writes whole
+        // 32-byte sectors: lane 2m+e writes region offset 16e + 32i at step i.
+        if (SECTOR_PAIRS) {
+            const bool odd = lane & 1;
+            uint32_t snd[8], rcv[8];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                float v[4];
-#pragma unroll
-                for (int b = 0; b < 4; ++b)
-                    v[b] = __fsub_rn(__fmul_rn(cdsc, static_cast<float>(byte_of(x[i], b))), cdm);
-                stg128f(dst + 4 * i, v[0], v[1], v[2], v[3]);
+                snd[i] = odd ? lo[i] : lo[4 + i];        // odd sends c0, even sends c1
+                snd[4 + i] = odd ? hi[i] : hi[4 + i];    // odd sends c2, even sends c3
             }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) rcv[i] = __shfl_xor_sync(kFull, snd[i], 1);
+            if (valid) {
+                uint8_t* base = D.codes + off - 64 * (odd ? 1 : 0) + 16 * (odd ? 1 : 0);
+                // even: c0, c2, partner c0, partner c2;  odd: partner c1, partner c3, c1, c3
+                uint4 v0 = odd ? make_uint4(rcv[0], rcv[1], rcv[2], rcv[3]) : make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                uint4 v1 = odd ? make_uint4(rcv[4], rcv[5], rcv[6], rcv[7]) : make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                uint4 v2 = odd ? make_uint4(lo[4], lo[5], lo[6], lo[7]) : make_uint4(rcv[0], rcv[1], rcv[2], rcv[3]);
+                uint4 v3 = odd ? make_uint4(hi[4], hi[5], hi[6], hi[7]) : make_uint4(rcv[4], rcv[5], rcv[6], rcv[7]);
+                stg128(base, v0);
+                stg128(base + 32, v1);
+                stg128(base + 64, v2);
+                stg128(base + 96, v3);
+            }
+        } else if (valid) {
+            uint8_t* base = D.codes + off;
+            stg128(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
+            stg128(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
+            stg128(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
+            stg128(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
+        }
+    }
+    if ((MODE & kOutF32) && valid) {
+        // gguf-py dequantize: (d*sc)*q - dmin*m, each product rounded (Q4_K/Q5_K.dequantize_blocks)
+        const float dsL = __fmul_rn(d, static_cast<float>(scL)), dmL = __fmul_rn(dmin, static_cast<float>(mnL));
+        const float dsH = __fmul_rn(d, static_cast<float>(scH)), dmH = __fmul_rn(dmin, static_cast<float>(mnH));
+        float* dst = D.values + off;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t ql = codes_word(EL[i], OL[i] >> 8);
+            const uint32_t qh = codes_word(EH[i] >> 4, OH[i] >> kOHShift);
+            stg128f(dst + 4 * i, __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 0))), dmL),
+                    __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 1))), dmL),
+                    __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 2))), dmL),
+                    __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 3))), dmL));
+            stg128f(dst + 32 + 4 * i, __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 0))), dmH),
+                    __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 1))), dmH),
+                    __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 2))), dmH),
+                    __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 3))), dmH));
         }
     }
 }
@@ -330,10 +430,11 @@ __global__ void __launch_bounds__(kThreads) gq_convert_kernel(const __grid_const
     const int64_t first = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
     const int64_t total = batch.total_tiles;
 
+    DescCursor issue_cur, proc_cur;
     int64_t t_issue = first;
 #pragma unroll
     for (int s = 0; s < F::kStages - 1; ++s) {
-        issue_tile<F>(batch, t_issue, ring + s * F::kStageBytes, lane);
+        issue_tile<F>(batch, issue_cur, t_issue, ring + s * F::kStageBytes, lane);
         cp_async_commit();
         t_issue += nwarps;
     }
@@ -345,18 +446,18 @@ __global__ void __launch_bounds__(kThreads) gq_convert_kernel(const __grid_const
         __syncwarp();
         // refill the stage consumed in the previous iteration
         const int refill = (stage == 0) ? F::kStages - 1 : stage - 1;
-        issue_tile<F>(batch, t_issue, ring + refill * F::kStageBytes, lane);
+        issue_tile<F>(batch, issue_cur, t_issue, ring + refill * F::kStageBytes, lane);
         cp_async_commit();
         t_issue += nwarps;
 
-        const GqDesc& D = batch.d[find_desc(batch, t)];
+        const GqDesc& D = batch.d[proc_cur.seek(batch, t)];
         const int64_t unit0 = (t - D.tile_begin) * F::kUnitsPerTile;
         const int64_t left = D.n_units - unit0;
         const int nunits = left < F::kUnitsPerTile ? static_cast<int>(left) : F::kUnitsPerTile;
         const uint8_t* tile = ring + stage * F::kStageBytes;
         if (TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K) {
             if (MODE & kOutCodes) acc.retarget(D.diag, lane);
-            process_q45k<TYPE == GQ_TYPE_Q5_K, MODE>(D, unit0, nunits, tile, lane, acc);
+            process_k45<TYPE == GQ_TYPE_Q5_K, MODE, false>(D, unit0, nunits, tile, lane, acc);
         } else if (TYPE == GQ_TYPE_Q6_K) {
             process_q6k<MODE>(D, unit0, nunits, tile, lane);
         } else {
