@@ -145,6 +145,29 @@ GQ_API int gq_session_destroy(gq_session_t* session);
 GQ_API int gq_convert_host(gq_session_t* session, const gq_tensor_t* tensors, int32_t count,
                     int32_t out_mask, gq_diag_t* host_diags);
 
+/* Allocation-free host-buffer conversion.  No counterpart in the reference: it exists for
+ * callers that must not allocate device memory while they prepare weights, e.g. a process
+ * whose device memory already belongs to another allocator (a framework's caching pool or
+ * a fixed budget shared with an inference runtime), where cudaMalloc can fail or stall the
+ * whole device.  Same inputs, outputs and results as gq_convert_host, but every byte of
+ * device staging lives in one fixed array inside the library, GQ_NOALLOC_SCRATCH_BYTES per
+ * GPU, held by every GPU that loads the library until the process exits; the call creates
+ * no streams or events and allocates no host or device memory.  Work runs on `stream`
+ * (NULL = legacy default stream), one piece at a time, and the call returns when the
+ * results are in host memory.
+ *   - The first call on a device looks up the array's device address (with `device`
+ *     made current); make that first call before any stream capture.
+ *   - Limits: the first 64 KiB of the array hold the diagnostics, so at most 8192 tensors
+ *     per call when host_diags is given; the rest stages one piece at a time, so a piece
+ *     of one unit (a head of rows for a permuted tensor) must fit.  Larger requests fail
+ *     with GQ_ERR_SIZE before any device work.
+ *   - All calls share the array.  Calls of this process on one device are serialized;
+ *     anything else that runs on the GPU at the same time as a call and touches the array
+ *     races with it. */
+#define GQ_NOALLOC_SCRATCH_BYTES (16u << 20)
+GQ_API int gq_convert_host_noalloc(int32_t device, const gq_tensor_t* tensors, int32_t count,
+                                   int32_t out_mask, gq_diag_t* host_diags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

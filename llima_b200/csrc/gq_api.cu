@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <new>
 #include <vector>
 
@@ -476,6 +477,182 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
         if (st != GQ_OK) return st;
     }
     return GQ_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free host-buffer conversion
+//
+// Some callers cannot allocate device memory at the point where they convert weights: a
+// process whose device memory is already handed out to another allocator (a framework's
+// caching pool, a fixed budget shared with a runtime) must not call cudaMalloc, because it
+// can fail there or implicitly synchronize the whole device.  For them this entry point
+// stages everything in one fixed device array that is part of the library image: no
+// cudaMalloc, cudaFree, stream or event creation, and no host heap allocation.
+// ---------------------------------------------------------------------------------------
+
+// The staging array.  Every GPU that loads the library holds these bytes until the
+// process exits.  The first kNoAllocDiagBytes hold the per-tensor diagnostics.
+constexpr size_t kNoAllocBytes = GQ_NOALLOC_SCRATCH_BYTES;
+constexpr size_t kNoAllocDiagBytes = size_t(64) << 10;
+static __device__ __align__(256) uint8_t gq_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+
+// Per-device state: the array's device address (set up once, with the device current)
+// and the batch parameter block, both in static storage.  The mutex serializes calls of
+// this process on one device; all of them share the array.
+struct NoAllocDevice {
+    std::mutex mu;
+    uint8_t* scratch = nullptr;
+    gq::GqBatch batch;
+};
+NoAllocDevice g_noalloc[64];
+
+int noalloc_setup(int device, NoAllocDevice** out) {
+    if (device < 0 || device >= 64) return GQ_ERR_ARG;
+    NoAllocDevice& nd = g_noalloc[device];
+    if (nd.scratch == nullptr) {
+        // In host code the symbol is only a stand-in: its device address must be asked
+        // for, once per device, while that device is current.
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, gq_noalloc_scratch);
+        if (e != cudaSuccess || ptr == nullptr) return cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+        nd.scratch = static_cast<uint8_t*>(ptr);
+    }
+    *out = &nd;
+    return GQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gq_convert_host_noalloc(int32_t device, const gq_tensor_t* tensors, int32_t count, int32_t out_mask,
+                            gq_diag_t* host_diags, void* stream) {
+    if (count < 0) return GQ_ERR_ARG;
+    if (count > 0 && tensors == nullptr) return GQ_ERR_NULL;
+    if (!valid_mask(out_mask)) return GQ_ERR_ARG;
+    if (host_diags != nullptr && static_cast<size_t>(count) * sizeof(gq_diag_t) > kNoAllocDiagBytes)
+        return GQ_ERR_SIZE;   // more tensors than the diagnostics area holds
+    if (device < 0 || device >= 64) return GQ_ERR_ARG;
+    const size_t staging = kNoAllocBytes - kNoAllocDiagBytes;
+    // validate everything before any device work
+    for (int i = 0; i < count; ++i) {
+        const gq_tensor_t& t = tensors[i];
+        TypeInfo ti;
+        int64_t nv = 0, nu = 0;
+        const int st = shape_check(t, &ti, &nv, &nu);
+        if (st != GQ_OK) return st;
+        if (nv == 0) continue;
+        if (t.src == nullptr) return GQ_ERR_NULL;
+        if (ti.block_values == 0) {
+            if (t.values == nullptr) return GQ_ERR_NULL;
+        } else {
+            if ((out_mask & GQ_OUT_CODES) && (t.codes == nullptr || t.scales == nullptr)) return GQ_ERR_NULL;
+            if ((out_mask & GQ_OUT_F32) && t.values == nullptr) return GQ_ERR_NULL;
+        }
+        // the smallest piece (one unit, or one head of a permuted tensor) must fit
+        const size_t fp = unit_footprint(ti, out_mask);
+        const int64_t upr = t.cols / ti.unit_values;
+        const int64_t min_units = t.perm_heads > 0 ? (t.rows / t.perm_heads) * upr : 1;
+        if (static_cast<size_t>(min_units) * fp + 4 * kAlign > staging) return GQ_ERR_SIZE;
+    }
+    int st = guard_device(device);
+    if (st != GQ_OK) return st;
+    NoAllocDevice* nd = nullptr;
+    std::lock_guard<std::mutex> lock(g_noalloc[device].mu);
+    if ((st = noalloc_setup(device, &nd)) != GQ_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    gq_diag_t* d_diag = reinterpret_cast<gq_diag_t*>(nd->scratch);
+    uint8_t* base = nd->scratch + kNoAllocDiagBytes;
+    if (host_diags != nullptr && count > 0) {
+        // the array keeps the previous call's contents: the maxima must start at zero
+        st = cuda_status(cudaMemsetAsync(d_diag, 0, sizeof(gq_diag_t) * count, s));
+        if (st != GQ_OK) return st;
+    }
+    gq::GqBatch& b = nd->batch;
+    for (int i = 0; i < count; ++i) {
+        const gq_tensor_t& t = tensors[i];
+        TypeInfo ti;
+        int64_t nv = 0, units = 0;
+        shape_check(t, &ti, &nv, &units);
+        if (nv == 0) continue;
+        const size_t fp = unit_footprint(ti, out_mask);
+        const int64_t upr = t.cols / ti.unit_values;
+        // a permuted tensor is cut into whole heads, which the permutation keeps apart
+        const int64_t step = t.perm_heads > 0 ? (t.rows / t.perm_heads) * upr : 1;
+        int64_t per_piece = static_cast<int64_t>((staging - 4 * kAlign) / fp);
+        per_piece = (per_piece / step) * step;
+        for (int64_t u0 = 0; u0 < units; u0 += per_piece) {
+            const int64_t n = std::min<int64_t>(per_piece, units - u0);
+            const int64_t nvals = n * ti.unit_values;
+            size_t off = 0;
+            gq_tensor_t dt = t;
+            dt.src = base;
+            dt.src_bytes = static_cast<size_t>(n) * ti.unit_bytes;
+            off = round_up(off + dt.src_bytes);
+            if (t.perm_heads > 0) {
+                dt.rows = n / upr;
+                dt.perm_heads = static_cast<int32_t>(dt.rows / (t.rows / t.perm_heads));
+            } else {
+                dt.rows = 1;
+                dt.cols = nvals;
+            }
+            dt.diag = host_diags ? d_diag + i : nullptr;
+            st = cuda_status(cudaMemcpyAsync(base, static_cast<const uint8_t*>(t.src) + u0 * ti.unit_bytes,
+                                             dt.src_bytes, cudaMemcpyHostToDevice, s));
+            if (st != GQ_OK) return st;
+            void* h_dst[3] = {nullptr, nullptr, nullptr};
+            const void* d_src[3] = {nullptr, nullptr, nullptr};
+            size_t n_bytes[3] = {0, 0, 0};
+            if (ti.block_values == 0) {
+                dt.values = reinterpret_cast<float*>(base + off);
+                n_bytes[0] = static_cast<size_t>(nvals) * ti.unit_bytes;
+                h_dst[0] = reinterpret_cast<uint8_t*>(t.values) + u0 * ti.unit_bytes;
+                d_src[0] = dt.values;
+            } else {
+                if (out_mask & GQ_OUT_CODES) {
+                    dt.codes = base + off;
+                    off = round_up(off + nvals);
+                    dt.scales = reinterpret_cast<float*>(base + off);
+                    const int64_t nsc = nvals / ti.block_values;
+                    off = round_up(off + 4 * nsc);
+                    h_dst[0] = static_cast<uint8_t*>(t.codes) + u0 * ti.unit_values;
+                    d_src[0] = dt.codes;
+                    n_bytes[0] = static_cast<size_t>(nvals);
+                    h_dst[1] = t.scales + u0 * (ti.unit_values / ti.block_values);
+                    d_src[1] = dt.scales;
+                    n_bytes[1] = static_cast<size_t>(4 * nsc);
+                }
+                if (out_mask & GQ_OUT_F32) {
+                    dt.values = reinterpret_cast<float*>(base + off);
+                    h_dst[2] = t.values + u0 * ti.unit_values;
+                    d_src[2] = dt.values;
+                    n_bytes[2] = static_cast<size_t>(4 * nvals);
+                }
+            }
+            b.n = 1;
+            b.total_tiles = gq::tiles_for(t.type, n);
+            b.d[0] = make_desc(dt, ti, n);
+            b.d[0].tile_begin = 0;
+            const int e = gq::launch_batch(t.type, out_mask, b, s);
+            if (e != 0) return cuda_status(e);
+            for (int k = 0; k < 3; ++k) {
+                if (n_bytes[k] == 0) continue;
+                st = cuda_status(cudaMemcpyAsync(h_dst[k], d_src[k], n_bytes[k], cudaMemcpyDeviceToHost, s));
+                if (st != GQ_OK) return st;
+            }
+            // the next piece overwrites the staging bytes: stream order puts its copy
+            // after these reads
+        }
+    }
+    if (host_diags != nullptr && count > 0) {
+        st = cuda_status(cudaMemcpyAsync(host_diags, d_diag, sizeof(gq_diag_t) * count, cudaMemcpyDeviceToHost, s));
+        if (st != GQ_OK) return st;
+    }
+    return cuda_status(cudaStreamSynchronize(s));
 }
 
 }  // extern "C"
