@@ -53,7 +53,7 @@ struct Requant {
 // for infinite or NaN r the product is NaN.  So numpy's int16(int32(rint(r*sf))) equals
 // cvt.rni (round half even, NaN -> 0) here, and no int16 sum can wrap.
 __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int qmax,
-                                                 int lo_out, int hi_out) {
+                                                 int lo_out, int hi_out, const float* recip = nullptr) {
     Requant p;
     const float s_eff = (S == 0.0f) ? ((fabsf(M) > kScaleEpsilon) ? M : kScaleEpsilon) : S;
     const float r = __fdiv_rn(M, s_eff);
@@ -61,12 +61,20 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     const float qmaxf = static_cast<float>(qmax);
     const float lo = __fadd_rn(qminf, r);
     const float hi = __fadd_rn(qmaxf, r);
+    // sf = min(16, lo_out/lo if lo < 0, hi_out/hi if hi > 0).  A quotient of 16 or more
+    // cannot lower sf, so only lo < lo_out/16 and hi > hi_out/16 matter; neither quotient
+    // can be NaN, so fminf matches np.minimum.  When both matter, the smaller one is found
+    // without dividing: lo_out/lo < hi_out/hi  <=>  lo_out*hi - hi_out*lo > 0 (lo < 0 < hi),
+    // whose sign one fma gives exactly (lo_out*hi is exact, |lo|, |hi| < 400 here), and
+    // since rounding is monotone the rounded quotient of the smaller one is the minimum.
+    const bool need_lo = lo < static_cast<float>(lo_out) / 16.0f;
+    const bool need_hi = hi > static_cast<float>(hi_out) / 16.0f;
     float sf = 16.0f;
-    // np.minimum(16, -128/lo) and np.minimum(sf, 127/hi).  Neither quotient can be NaN
-    // here (lo < 0 and hi > 0 exclude NaN), so fminf matches np.minimum.  A quotient of
-    // 16 or more cannot lower sf, so the division is skipped exactly then.
-    if (lo < static_cast<float>(lo_out) / 16.0f) sf = fminf(sf, __fdiv_rn(static_cast<float>(lo_out), lo));
-    if (hi > static_cast<float>(hi_out) / 16.0f) sf = fminf(sf, __fdiv_rn(static_cast<float>(hi_out), hi));
+    if (need_lo || need_hi) {
+        const float e = __fmaf_rn(-static_cast<float>(hi_out), lo, __fmul_rn(static_cast<float>(lo_out), hi));
+        const bool use_lo = need_lo && (!need_hi || e > 0.0f);
+        sf = fminf(sf, __fdiv_rn(static_cast<float>(use_lo ? lo_out : hi_out), use_lo ? lo : hi));
+    }
     const bool big = sf > 0.98f;
     if (big) sf = fmaxf(floorf(sf), 1.0f);
     const float rmv = __fmul_rn(r, sf);
@@ -74,7 +82,6 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     p.sf = sf;
     p.rm = rm;
     p.round_err = fabsf(__fsub_rn(rintf(rmv), rmv));
-    p.scale = __fdiv_rn(S, sf);
     p.fast = big || (sf == 0.0f);
     int vmin, vmax;
     if (p.fast) {
@@ -85,6 +92,17 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
         p.sfi = 0;
         vmin = __float2int_rn(__fmul_rn(qminf, sf)) + rm;
         vmax = __float2int_rn(__fmul_rn(qmaxf, sf)) + rm;
+    }
+    // scale = S / sf (the original S, ggml_quant.py:882).  For an integer sf in 1..16 and a
+    // finite S: q0 = S*(1/sf) and one fma correction, which equals IEEE division for every
+    // f16-derived S (checked exhaustively, tests/numerics/div_by_small_int.c).
+    if (recip != nullptr && big && fabsf(S) < __int_as_float(0x7f800000)) {
+        const float y = recip[p.sfi];
+        const float q0 = __fmul_rn(S, y);
+        const float res = __fmaf_rn(-sf, q0, S);
+        p.scale = (res == 0.0f) ? q0 : __fmaf_rn(res, y, q0);
+    } else {
+        p.scale = __fdiv_rn(S, sf);
     }
     // q' is monotone in q (sf >= 0), so the block's extreme codes bound every code's clipping.
     p.clip = (vmax > hi_out) || (vmin < lo_out);

@@ -27,6 +27,17 @@ namespace gq {
 // Format geometry: stored unit size, units per tile, pipeline depth
 // ---------------------------------------------------------------------------------------
 
+// Groups of 32 nibble bytes per lane in a Q4_K / Q5_K tile, and the pipeline depth.
+#ifndef GQ_K45_GROUPS
+#define GQ_K45_GROUPS 1
+#endif
+#ifndef GQ_Q5K_GROUPS
+#define GQ_Q5K_GROUPS 1
+#endif
+#ifndef GQ_K45_STAGES
+#define GQ_K45_STAGES 4
+#endif
+
 template <int TYPE>
 struct Fmt;
 
@@ -41,12 +52,18 @@ struct Fmt;
         static_assert(kTileBytes % 16 == 0, "tiles must be whole 16-byte chunks");        \
     };
 
-GQ_FMT(GQ_TYPE_Q4_K, 144, 8, 4)   // 64 blocks of 32 per tile: one 32-byte group per lane
-GQ_FMT(GQ_TYPE_Q5_K, 176, 8, 4)
+GQ_FMT(GQ_TYPE_Q4_K, 144, 8 * GQ_K45_GROUPS, GQ_K45_STAGES)   // lane: GQ_K45_GROUPS 32-byte groups
+GQ_FMT(GQ_TYPE_Q5_K, 176, 8 * GQ_Q5K_GROUPS, GQ_K45_STAGES)
 GQ_FMT(GQ_TYPE_Q6_K, 210, 8, 3)   // 128 blocks of 16 per tile
 GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4)   // 32 blocks of 32 per tile
 GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4)
 #undef GQ_FMT
+
+// Minimum resident CTAs per SM the Q4_K kernel is compiled for (caps its registers; the
+// other formats leave the register count to the compiler).
+#ifndef GQ_MIN_BLOCKS
+#define GQ_MIN_BLOCKS 3
+#endif
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
@@ -124,194 +141,226 @@ __device__ __forceinline__ uint32_t requant_word_general(uint32_t q4, const Requ
     return requant_word_slow(q4, p.sf, p.rm, -128, 127);
 }
 
-template <bool Q5, int MODE, bool SECTOR_PAIRS>
-__device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int nunits,
-                                            const uint8_t* tile, int lane, DiagAcc& acc) {
-    constexpr int UB = Q5 ? 176 : 144;
-    constexpr int QS = Q5 ? 48 : 16;   // offset of the nibble bytes
-    const int sb = lane >> 2;
-    const int g = lane & 3;
-    const bool valid = sb < nunits;
-    const uint8_t* sbp = tile + sb * UB;
+// The 32 code bytes of one group (and Q5_K's fifth-bit bytes, pre-shifted so that bit 0
+// of each byte is the fifth bit of the low-nibble block).
+template <bool Q5>
+struct GroupWords {
+    uint32_t w[8];
+    uint32_t h[Q5 ? 8 : 1];
+};
 
-    // ---- 6-bit scale / min of blocks 2g and 2g+1 (ggml_quant.py:352-375): byte j of the
-    // first / second / third word of the 12 scale bytes, for j = (2g)&3 and (2g)&3 + 1
-    const uint32_t hdr = lds32(sbp);
-    const uint32_t sel = (g & 1) ? 0x4432u : 0x4410u;
-    const uint32_t b0 = __byte_perm(lds32(sbp + 4), 0, sel);
-    const uint32_t b1 = __byte_perm(lds32(sbp + 8), 0, sel);
-    const uint32_t b2 = __byte_perm(lds32(sbp + 12), 0, sel);
-    const uint32_t sc2 = (g < 2) ? (b0 & 0x3F3Fu) : ((b2 & 0x0F0Fu) | ((b0 >> 2) & 0x3030u));
-    const uint32_t mn2 = (g < 2) ? (b1 & 0x3F3Fu) : (((b2 >> 4) & 0x0F0Fu) | ((b1 >> 2) & 0x3030u));
-    const float d = h2f(hdr);
-    const float dmin = h2f(hdr >> 16);
-    const int scL = sc2 & 0xFF, scH = sc2 >> 8, mnL = mn2 & 0xFF, mnH = mn2 >> 8;
+// a & m that the compiler may not merge with an equal expression elsewhere: the masks are
+// recomputed where they are used instead of being kept live across the requantization
+__device__ __forceinline__ uint32_t and_fresh(uint32_t a, uint32_t m) {
+    uint32_t r;
+    asm volatile("and.b32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(m));
+    return r;
+}
 
-    // ---- the group's 32 code bytes in the four lane layouts
-    const uint8_t* qp = sbp + QS + 32 * g;
-    const uint4 qa = lds128(qp), qb = lds128(qp + 16);
-    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    uint32_t EL[8], OL[8], EH[8], OH[8];
+// The four 16-bit lane layouts of word i (see above).  FRESH: recompute (apply phase).
+template <bool Q5, bool FRESH = false>
+__device__ __forceinline__ void group_layouts(const GroupWords<Q5>& q, int i, uint32_t& el, uint32_t& ol,
+                                              uint32_t& eh, uint32_t& oh) {
+    const uint32_t w = q.w[i];
     if (!Q5) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            EL[i] = w[i] & 0x000F000Fu;
-            OL[i] = w[i] & 0x0F000F00u;
-            EH[i] = w[i] & 0x00F000F0u;
-            OH[i] = w[i] & 0xF000F000u;
+        if (FRESH) {
+            el = and_fresh(w, 0x000F000Fu);
+            ol = and_fresh(w, 0x0F000F00u);
+            eh = and_fresh(w, 0x00F000F0u);
+            oh = and_fresh(w, 0xF000F000u);
+        } else {
+            el = w & 0x000F000Fu;
+            ol = w & 0x0F000F00u;
+            eh = w & 0x00F000F0u;
+            oh = w & 0xF000F000u;
         }
     } else {
-        // fifth bit of block k is bit k of qh[j] (ggml_quant.py:311-349): bit 2g for the
-        // low nibbles, 2g+1 for the high nibbles
-        const uint4 ha = lds128(sbp + 16), hb = lds128(sbp + 32);
-        const uint32_t h[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t t = h[i] >> (2 * g);
-            const uint32_t t4 = t << 4;
-            EL[i] = (w[i] & 0x000F000Fu) | (t4 & 0x00100010u);
-            OL[i] = (w[i] & 0x0F000F00u) | (t4 & 0x10001000u);
-            EH[i] = (w[i] & 0x00F000F0u) | ((t << 7) & 0x01000100u);
-            OH[i] = ((w[i] >> 12) & 0x000F000Fu) | ((t >> 5) & 0x00100010u);
-        }
+        const uint32_t t = q.h[Q5 ? i : 0], t4 = t << 4;
+        el = (w & 0x000F000Fu) | (t4 & 0x00100010u);
+        ol = (w & 0x0F000F00u) | (t4 & 0x10001000u);
+        eh = (w & 0x00F000F0u) | ((t << 7) & 0x01000100u);
+        oh = ((w >> 12) & 0x000F000Fu) | ((t >> 5) & 0x00100010u);
     }
+}
+
+// A lane owns G groups: group j is super-block lane/4 + 8j, group g = lane%4 of it.  The
+// min/max scans of all groups come first, then the 2G independent requantization chains
+// (long dependent sequences of divisions and roundings) are issued together so that they
+// hide each other's latency, then each group is requantized from its raw words.
+template <bool Q5, int MODE, int G>
+__device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int nunits,
+                                            const uint8_t* tile, int lane, DiagAcc& acc,
+                                            const float* recip) {
+    constexpr int UB = Q5 ? 176 : 144;
+    constexpr int QS = Q5 ? 48 : 16;   // offset of the nibble bytes
     constexpr int kOHShift = Q5 ? 0 : 12;
+    const int g = lane & 3;
+    const uint32_t sel = (g & 1) ? 0x4432u : 0x4410u;
 
-    Requant pL{}, pH{};
-    if (MODE & kOutCodes) {
-        // ---- block min / max of the codes (16-bit-lane SIMD)
-        uint32_t mnEL = vmin16(EL[0], EL[1], EL[2]), mxEL = vmax16(EL[0], EL[1], EL[2]);
-        uint32_t mnOL = vmin16(OL[0], OL[1], OL[2]), mxOL = vmax16(OL[0], OL[1], OL[2]);
-        uint32_t mnEH = vmin16(EH[0], EH[1], EH[2]), mxEH = vmax16(EH[0], EH[1], EH[2]);
-        uint32_t mnOH = vmin16(OH[0], OH[1], OH[2]), mxOH = vmax16(OH[0], OH[1], OH[2]);
+    GroupWords<Q5> q[G];
+    int scL[G], scH[G], mnL[G], mnH[G];
+    float d[G], dmin[G];
+    bool valid[G];
 #pragma unroll
-        for (int i = 3; i < 8; i += 2) {
-            const int j = i + 1 < 8 ? i + 1 : i;
-            mnEL = vmin16(mnEL, EL[i], EL[j]);
-            mxEL = vmax16(mxEL, EL[i], EL[j]);
-            mnOL = vmin16(mnOL, OL[i], OL[j]);
-            mxOL = vmax16(mxOL, OL[i], OL[j]);
-            mnEH = vmin16(mnEH, EH[i], EH[j]);
-            mxEH = vmax16(mxEH, EH[i], EH[j]);
-            mnOH = vmin16(mnOH, OH[i], OH[j]);
-            mxOH = vmax16(mxOH, OH[i], OH[j]);
+    for (int j = 0; j < G; ++j) {
+        const int sb = (lane >> 2) + 8 * j;
+        valid[j] = sb < nunits;
+        const uint8_t* sbp = tile + sb * UB;
+        // 6-bit scale / min of blocks 2g and 2g+1 (ggml_quant.py:352-375): byte j' of the
+        // first / second / third word of the 12 scale bytes, j' = (2g)&3 and (2g)&3 + 1
+        const uint32_t hdr = lds32(sbp);
+        const uint32_t b0 = __byte_perm(lds32(sbp + 4), 0, sel);
+        const uint32_t b1 = __byte_perm(lds32(sbp + 8), 0, sel);
+        const uint32_t b2 = __byte_perm(lds32(sbp + 12), 0, sel);
+        const uint32_t sc2 = (g < 2) ? (b0 & 0x3F3Fu) : ((b2 & 0x0F0Fu) | ((b0 >> 2) & 0x3030u));
+        const uint32_t mn2 = (g < 2) ? (b1 & 0x3F3Fu) : (((b2 >> 4) & 0x0F0Fu) | ((b1 >> 2) & 0x3030u));
+        d[j] = h2f(hdr);
+        dmin[j] = h2f(hdr >> 16);
+        scL[j] = sc2 & 0xFF;
+        scH[j] = sc2 >> 8;
+        mnL[j] = mn2 & 0xFF;
+        mnH[j] = mn2 >> 8;
+        const uint8_t* qp = sbp + QS + 32 * g;
+        const uint4 qa = lds128(qp), qb = lds128(qp + 16);
+        q[j].w[0] = qa.x; q[j].w[1] = qa.y; q[j].w[2] = qa.z; q[j].w[3] = qa.w;
+        q[j].w[4] = qb.x; q[j].w[5] = qb.y; q[j].w[6] = qb.z; q[j].w[7] = qb.w;
+        if (Q5) {
+            // fifth bit of block k is bit k of qh[j] (ggml_quant.py:311-349): bit 2g for the
+            // low nibbles, 2g+1 for the high nibbles
+            const uint4 ha = lds128(sbp + 16), hb = lds128(sbp + 32);
+            const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[j].h[Q5 ? i : 0] = hw[i] >> (2 * g);
         }
-        const uint32_t aminL = vmin16(mnEL, mnOL >> 8), amaxL = vmax16(mxEL, mxOL >> 8);
-        const uint32_t aminH = vmin16(mnEH >> 4, mnOH >> kOHShift), amaxH = vmax16(mxEH >> 4, mxOH >> kOHShift);
-        const int qminL = min(aminL & 0xFFFF, aminL >> 16), qmaxL = max(amaxL & 0xFFFF, amaxL >> 16);
-        const int qminH = min(aminH & 0xFFFF, aminH >> 16), qmaxH = max(amaxH & 0xFFFF, amaxH >> 16);
-
-        // ---- block constants f16(f32 product), min negated (ggml_quant.py:771-777), then
-        // requantize_symmetric (ggml_quant.py:785-886)
-        const float SL = round_to_f16(__fmul_rn(static_cast<float>(scL), d));
-        const float SH = round_to_f16(__fmul_rn(static_cast<float>(scH), d));
-        const float ML = -round_to_f16(__fmul_rn(static_cast<float>(mnL), dmin));
-        const float MH = -round_to_f16(__fmul_rn(static_cast<float>(mnH), dmin));
-        pL = requant_block(SL, ML, qminL, qmaxL, -128, 127);
-        pH = requant_block(SH, MH, qminH, qmaxH, -128, 127);
     }
 
-    const int64_t ou = permute_unit(D, unit0 + sb);
-    const int64_t off = ou * 256 + 64 * g;   // codes / values of block 2g, then 2g+1
-
+    Requant pL[G], pH[G];
     if (MODE & kOutCodes) {
-        if (valid) {
-            *reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g) = make_float2(pL.scale, pH.scale);
-            acc.add(pL.round_err, pL.clip_err);
-            acc.add(pH.round_err, pH.clip_err);
-        }
-        uint32_t lo[8], hi[8];
-        constexpr uint32_t kBias = 0x400u;   // lane value q*sf + rm + bias stays in [0, 4096)
-        constexpr uint32_t kLo2 = (kBias - 128u) * 0x00010001u, kHi2 = (kBias + 127u) * 0x00010001u;
-        const uint32_t sfiL = static_cast<uint32_t>(pL.sfi), sfiH = static_cast<uint32_t>(pH.sfi);
-        const uint32_t KL = static_cast<uint32_t>(pL.rm + static_cast<int>(kBias)) * 0x00010001u;
-        const uint32_t KH = static_cast<uint32_t>(pH.rm + static_cast<int>(kBias)) * 0x00010001u;
-        const bool plainL = pL.fast && !pL.clip, plainH = pH.fast && !pH.clip;
+        int qminL[G], qmaxL[G], qminH[G], qmaxH[G];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            // low nibbles: EL * sf + K and high32(OL * (sf << 24)) + K; high nibbles:
-            // (EH * sf + 16K) >> 4 and high32(OH * (sf << 20)) + K (Q5_K: OH * sf + K)
-            lo[i] = codes_word(EL[i] * sfiL + KL, mad_hi(OL[i], sfiL << 24, KL));
-            const uint32_t eh = (EH[i] * sfiH + (KH << 4)) >> 4;
-            const uint32_t oh = Q5 ? OH[i] * sfiH + KH : mad_hi(OH[i], sfiH << 20, KH);
-            hi[i] = codes_word(eh, oh);
-        }
-        if (!plainL) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (pL.fast) {
-                    const uint32_t e = vmin16(vmax16(EL[i] * sfiL + KL, kLo2), kHi2);
-                    const uint32_t o = vmin16(vmax16(mad_hi(OL[i], sfiL << 24, KL), kLo2), kHi2);
-                    lo[i] = codes_word(e, o);
-                } else {
-                    lo[i] = requant_word_general(codes_word(EL[i], OL[i] >> 8), pL);
-                }
-            }
-        }
-        if (!plainH) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (pH.fast) {
-                    const uint32_t e = vmin16(vmax16((EH[i] * sfiH + (KH << 4)) >> 4, kLo2), kHi2);
-                    const uint32_t oh = Q5 ? OH[i] * sfiH + KH : mad_hi(OH[i], sfiH << 20, KH);
-                    const uint32_t o = vmin16(vmax16(oh, kLo2), kHi2);
-                    hi[i] = codes_word(e, o);
-                } else {
-                    hi[i] = requant_word_general(codes_word(EH[i] >> 4, OH[i] >> kOHShift), pH);
-                }
-            }
-        }
-        // 64 output bytes per lane as four 16-byte chunks c0..c3 (c0,c1: block 2g; c2,c3:
-        // block 2g+1).  With SECTOR_PAIRS, lanes 2m and 2m+1 (adjacent 64-byte regions of
-        // one super-block) swap chunks so that every store instruction writes whole
-        // 32-byte sectors: lane 2m+e writes region offset 16e + 32i at step i.
-        if (SECTOR_PAIRS) {
-            const bool odd = lane & 1;
-            uint32_t snd[8], rcv[8];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                snd[i] = odd ? lo[i] : lo[4 + i];        // odd sends c0, even sends c1
-                snd[4 + i] = odd ? hi[i] : hi[4 + i];    // odd sends c2, even sends c3
+        for (int j = 0; j < G; ++j) {
+            // block min / max of the codes (16-bit-lane SIMD), two words per step
+            uint32_t mnEL, mxEL, mnOL, mxOL, mnEH, mxEH, mnOH, mxOH;
+            {
+                uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
+                group_layouts(q[j], 0, a0, a1, a2, a3);
+                group_layouts(q[j], 1, c0, c1, c2, c3);
+                mnEL = vmin16(a0, c0); mxEL = vmax16(a0, c0);
+                mnOL = vmin16(a1, c1); mxOL = vmax16(a1, c1);
+                mnEH = vmin16(a2, c2); mxEH = vmax16(a2, c2);
+                mnOH = vmin16(a3, c3); mxOH = vmax16(a3, c3);
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) rcv[i] = __shfl_xor_sync(kFull, snd[i], 1);
-            if (valid) {
-                uint8_t* base = D.codes + off - 64 * (odd ? 1 : 0) + 16 * (odd ? 1 : 0);
-                // even: c0, c2, partner c0, partner c2;  odd: partner c1, partner c3, c1, c3
-                uint4 v0 = odd ? make_uint4(rcv[0], rcv[1], rcv[2], rcv[3]) : make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                uint4 v1 = odd ? make_uint4(rcv[4], rcv[5], rcv[6], rcv[7]) : make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                uint4 v2 = odd ? make_uint4(lo[4], lo[5], lo[6], lo[7]) : make_uint4(rcv[0], rcv[1], rcv[2], rcv[3]);
-                uint4 v3 = odd ? make_uint4(hi[4], hi[5], hi[6], hi[7]) : make_uint4(rcv[4], rcv[5], rcv[6], rcv[7]);
-                stg128(base, v0);
-                stg128(base + 32, v1);
-                stg128(base + 64, v2);
-                stg128(base + 96, v3);
+            for (int i = 2; i < 8; i += 2) {
+                uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
+                group_layouts(q[j], i, a0, a1, a2, a3);
+                group_layouts(q[j], i + 1, c0, c1, c2, c3);
+                mnEL = vmin16(mnEL, a0, c0); mxEL = vmax16(mxEL, a0, c0);
+                mnOL = vmin16(mnOL, a1, c1); mxOL = vmax16(mxOL, a1, c1);
+                mnEH = vmin16(mnEH, a2, c2); mxEH = vmax16(mxEH, a2, c2);
+                mnOH = vmin16(mnOH, a3, c3); mxOH = vmax16(mxOH, a3, c3);
             }
-        } else if (valid) {
-            uint8_t* base = D.codes + off;
-            stg128(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
-            stg128(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
-            stg128(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
-            stg128(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
+            const uint32_t aminL = vmin16(mnEL, mnOL >> 8), amaxL = vmax16(mxEL, mxOL >> 8);
+            const uint32_t aminH = vmin16(mnEH >> 4, mnOH >> kOHShift);
+            const uint32_t amaxH = vmax16(mxEH >> 4, mxOH >> kOHShift);
+            qminL[j] = min(aminL & 0xFFFF, aminL >> 16);
+            qmaxL[j] = max(amaxL & 0xFFFF, amaxL >> 16);
+            qminH[j] = min(aminH & 0xFFFF, aminH >> 16);
+            qmaxH[j] = max(amaxH & 0xFFFF, amaxH >> 16);
+        }
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+            // block constants f16(f32 product), min negated (ggml_quant.py:771-777), then
+            // requantize_symmetric (ggml_quant.py:785-886)
+            const float SL = round_to_f16(__fmul_rn(static_cast<float>(scL[j]), d[j]));
+            const float SH = round_to_f16(__fmul_rn(static_cast<float>(scH[j]), d[j]));
+            const float ML = -round_to_f16(__fmul_rn(static_cast<float>(mnL[j]), dmin[j]));
+            const float MH = -round_to_f16(__fmul_rn(static_cast<float>(mnH[j]), dmin[j]));
+            pL[j] = requant_block(SL, ML, qminL[j], qmaxL[j], -128, 127, recip);
+            pH[j] = requant_block(SH, MH, qminH[j], qmaxH[j], -128, 127, recip);
         }
     }
-    if ((MODE & kOutF32) && valid) {
-        // gguf-py dequantize: (d*sc)*q - dmin*m, each product rounded (Q4_K/Q5_K.dequantize_blocks)
-        const float dsL = __fmul_rn(d, static_cast<float>(scL)), dmL = __fmul_rn(dmin, static_cast<float>(mnL));
-        const float dsH = __fmul_rn(d, static_cast<float>(scH)), dmH = __fmul_rn(dmin, static_cast<float>(mnH));
-        float* dst = D.values + off;
+
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t ql = codes_word(EL[i], OL[i] >> 8);
-            const uint32_t qh = codes_word(EH[i] >> 4, OH[i] >> kOHShift);
-            stg128f(dst + 4 * i, __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 0))), dmL),
-                    __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 1))), dmL),
-                    __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 2))), dmL),
-                    __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 3))), dmL));
-            stg128f(dst + 32 + 4 * i, __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 0))), dmH),
-                    __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 1))), dmH),
-                    __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 2))), dmH),
-                    __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 3))), dmH));
+    for (int j = 0; j < G; ++j) {
+        const int sb = (lane >> 2) + 8 * j;
+        const int64_t ou = permute_unit(D, unit0 + sb);
+        const int64_t off = ou * 256 + 64 * g;   // codes / values of block 2g, then 2g+1
+        if (MODE & kOutCodes) {
+            if (valid[j]) {
+                *reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g) = make_float2(pL[j].scale, pH[j].scale);
+                acc.add(pL[j].round_err, pL[j].clip_err);
+                acc.add(pH[j].round_err, pH[j].clip_err);
+            }
+            constexpr uint32_t kBias = 0x400u;   // lane value q*sf + rm + bias stays in [0, 4096)
+            constexpr uint32_t kLo2 = (kBias - 128u) * 0x00010001u, kHi2 = (kBias + 127u) * 0x00010001u;
+            const uint32_t sfiL = static_cast<uint32_t>(pL[j].sfi), sfiH = static_cast<uint32_t>(pH[j].sfi);
+            const uint32_t KL = static_cast<uint32_t>(pL[j].rm + static_cast<int>(kBias)) * 0x00010001u;
+            const uint32_t KH = static_cast<uint32_t>(pH[j].rm + static_cast<int>(kBias)) * 0x00010001u;
+            const bool plain = pL[j].fast && !pL[j].clip && pH[j].fast && !pH[j].clip;
+            uint32_t lo[8], hi[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                // low nibbles: EL*sf + K and high32(OL * (sf << 24)) + K; high nibbles:
+                // (EH*sf + 16K) >> 4 and high32(OH * (sf << 20)) + K (Q5_K: OH*sf + K); the
+                // low bytes of the 16-bit lanes are the codes (the bias has a zero low byte)
+                uint32_t el, ol, eh, oh;
+                group_layouts<Q5, true>(q[j], i, el, ol, eh, oh);
+                lo[i] = codes_word(el * sfiL + KL, mad_hi(ol, sfiL << 24, KL));
+                hi[i] = codes_word((eh * sfiH + (KH << 4)) >> 4, Q5 ? oh * sfiH + KH : mad_hi(oh, sfiH << 20, KH));
+            }
+            if (!plain) {
+                // clipping or a non-integer scale factor (rare): redo the affected side
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    uint32_t el, ol, eh, oh;
+                    group_layouts<Q5, true>(q[j], i, el, ol, eh, oh);
+                    if (!pL[j].fast) {
+                        lo[i] = requant_word_general(codes_word(el, ol >> 8), pL[j]);
+                    } else if (pL[j].clip) {
+                        lo[i] = codes_word(vmin16(vmax16(el * sfiL + KL, kLo2), kHi2),
+                                           vmin16(vmax16(mad_hi(ol, sfiL << 24, KL), kLo2), kHi2));
+                    }
+                    if (!pH[j].fast) {
+                        hi[i] = requant_word_general(codes_word(eh >> 4, oh >> kOHShift), pH[j]);
+                    } else if (pH[j].clip) {
+                        const uint32_t ohv = Q5 ? oh * sfiH + KH : mad_hi(oh, sfiH << 20, KH);
+                        hi[i] = codes_word(vmin16(vmax16((eh * sfiH + (KH << 4)) >> 4, kLo2), kHi2),
+                                           vmin16(vmax16(ohv, kLo2), kHi2));
+                    }
+                }
+            }
+            if (valid[j]) {
+                uint8_t* base = D.codes + off;
+                stg128(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
+                stg128(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
+                stg128(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
+                stg128(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
+            }
+        }
+        if ((MODE & kOutF32) && valid[j]) {
+            // gguf-py dequantize: (d*sc)*q - dmin*m, each product rounded
+            // (Q4_K/Q5_K.dequantize_blocks)
+            const float dsL = __fmul_rn(d[j], static_cast<float>(scL[j]));
+            const float dmL = __fmul_rn(dmin[j], static_cast<float>(mnL[j]));
+            const float dsH = __fmul_rn(d[j], static_cast<float>(scH[j]));
+            const float dmH = __fmul_rn(dmin[j], static_cast<float>(mnH[j]));
+            float* vdst = D.values + off;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                uint32_t el, ol, eh, oh;
+                group_layouts<Q5, true>(q[j], i, el, ol, eh, oh);
+                const uint32_t ql = codes_word(el, ol >> 8);
+                const uint32_t qh = codes_word(eh >> 4, oh >> kOHShift);
+                stg128f(vdst + 4 * i, __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 0))), dmL),
+                        __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 1))), dmL),
+                        __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 2))), dmL),
+                        __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 3))), dmL));
+                stg128f(vdst + 32 + 4 * i, __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 0))), dmH),
+                        __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 1))), dmH),
+                        __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 2))), dmH),
+                        __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 3))), dmH));
+            }
         }
     }
 }
@@ -420,9 +469,13 @@ __device__ __forceinline__ void process_q0(const GqDesc& D, int64_t unit0, int n
 // ---------------------------------------------------------------------------------------
 
 template <int TYPE, int MODE>
-__global__ void __launch_bounds__(kThreads) gq_convert_kernel(const __grid_constant__ GqBatch batch) {
+__global__ void __launch_bounds__(kThreads, TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS : (TYPE == GQ_TYPE_Q5_K ? 2 : 1)) gq_convert_kernel(const __grid_constant__ GqBatch batch) {
     using F = Fmt<TYPE>;
     extern __shared__ __align__(16) uint8_t smem[];
+    // exact reciprocals 1/k, k = 1..16, for the block-scale division of requant_block
+    __shared__ float recip[17];
+    if (threadIdx.x < 17) recip[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, static_cast<float>(threadIdx.x)) : 0.0f;
+    __syncthreads();
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     uint8_t* ring = smem + warp * (F::kStages * F::kStageBytes);
@@ -457,7 +510,8 @@ __global__ void __launch_bounds__(kThreads) gq_convert_kernel(const __grid_const
         const uint8_t* tile = ring + stage * F::kStageBytes;
         if (TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K) {
             if (MODE & kOutCodes) acc.retarget(D.diag, lane);
-            process_k45<TYPE == GQ_TYPE_Q5_K, MODE, false>(D, unit0, nunits, tile, lane, acc);
+            process_k45<TYPE == GQ_TYPE_Q5_K, MODE, TYPE == GQ_TYPE_Q5_K ? GQ_Q5K_GROUPS : GQ_K45_GROUPS>(
+                D, unit0, nunits, tile, lane, acc, recip);
         } else if (TYPE == GQ_TYPE_Q6_K) {
             process_q6k<MODE>(D, unit0, nunits, tile, lane);
         } else {
@@ -569,12 +623,14 @@ template <int TYPE, int MODE>
 int launch_fmt(const GqBatch& b, cudaStream_t s) {
     using F = Fmt<TYPE>;
     constexpr int smem = kWarps * F::kStages * F::kStageBytes;
-    static_assert(smem <= 48 * 1024, "stay within the default dynamic shared memory limit");
+    static_assert(smem <= 200 * 1024, "dynamic shared memory per CTA");
     static int per_sm[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     int& occ = per_sm[dev & 63];
     if (occ == 0) {
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(gq_convert_kernel<TYPE, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gq_convert_kernel<TYPE, MODE>, kThreads, smem) !=
                 cudaSuccess || occ < 1)
             occ = 1;

@@ -151,9 +151,10 @@ MODEL_SETS: dict[str, ModelShape] = {
 }
 
 
-def model_specs(model: str, seed: int = 0) -> list[TensorSpec]:
-    """Tensor list of a model-shaped set, in GGUF file order."""
-    m = MODEL_SETS[model]
+def model_specs(model: "str | ModelShape", seed: int = 0) -> list[TensorSpec]:
+    """Tensor list of a model-shaped set (a MODEL_SETS name or a ModelShape), in GGUF
+    file order."""
+    m = MODEL_SETS[model] if isinstance(model, str) else model
     q_rows = m.n_head * m.head_dim
     kv_rows = m.n_kv * m.head_dim
     specs: list[TensorSpec] = []
@@ -182,12 +183,14 @@ def model_specs(model: str, seed: int = 0) -> list[TensorSpec]:
     return specs
 
 
-def head_count_for(model: str, tensor_name: str) -> int:
+def head_count_for(model: "str | ModelShape", tensor_name: str, llama: bool | None = None) -> int:
     """Heads of the Llama q/k row permutation (0 when the tensor is not permuted).
     ``sima_lmm/gguf/gguf_conversion.py:291-299`` applies it to attn_q/attn_k of llama models."""
-    if not model.startswith("llama"):
+    if llama is None:
+        llama = isinstance(model, str) and model.startswith("llama")
+    if not llama:
         return 0
-    m = MODEL_SETS[model]
+    m = MODEL_SETS[model] if isinstance(model, str) else model
     if tensor_name.endswith(("attn_q.weight", "attn_q.bias")):
         return m.n_head
     if tensor_name.endswith(("attn_k.weight", "attn_k.bias")):
