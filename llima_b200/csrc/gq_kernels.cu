@@ -67,7 +67,7 @@ GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4)
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr unsigned kFull = 0xffffffffu;
+[[maybe_unused]] constexpr unsigned kFull = 0xffffffffu;
 
 // Tensor owning global tile `t` (binary search over tile_begin).
 __device__ __forceinline__ int find_desc(const GqBatch& b, int64_t t) {
