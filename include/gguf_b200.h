@@ -9,6 +9,10 @@
  *   Q4_K, Q5_K -> f32 scales (per 32) + int8 codes, through the asymmetric -> symmetric
  *                 requantization (unpack_k_quant + convert_to_simple_block_quant)
  *   Q6_K -> f32 scales (per 16) + int8 codes                   (same path, no requant)
+ *   Q5_0 -> f32 scales (per 32) + int8 codes q - 16           (unpack_q5, SYMMETRIC)
+ *   Q4_1, Q5_1 -> f32 scales (per 32) + int8 codes via requantize_symmetric
+ *   Q2_K -> f32 scales (per 16) + int8 codes via the K-quant requantization
+ *   Q3_K -> f32 scales (per 16) + int8 codes q - 4
  *   F32 / F16 / BF16 -> copied unchanged
  *
  * and, on request, into f32 values exactly as gguf-py's dequantize computes them (the
@@ -61,7 +65,12 @@ extern "C" {
 #define GQ_TYPE_F32 0
 #define GQ_TYPE_F16 1
 #define GQ_TYPE_Q4_0 2
+#define GQ_TYPE_Q4_1 3
+#define GQ_TYPE_Q5_0 6
+#define GQ_TYPE_Q5_1 7
 #define GQ_TYPE_Q8_0 8
+#define GQ_TYPE_Q2_K 10
+#define GQ_TYPE_Q3_K 11
 #define GQ_TYPE_Q4_K 12
 #define GQ_TYPE_Q5_K 13
 #define GQ_TYPE_Q6_K 14

@@ -39,6 +39,11 @@ bool type_info(int type, TypeInfo* ti) {
         case GQ_TYPE_Q4_K: *ti = {256, 144, 32, true}; return true;
         case GQ_TYPE_Q5_K: *ti = {256, 176, 32, true}; return true;
         case GQ_TYPE_Q6_K: *ti = {256, 210, 16, false}; return true;
+        case GQ_TYPE_Q4_1: *ti = {32, 20, 32, true}; return true;
+        case GQ_TYPE_Q5_0: *ti = {32, 22, 32, false}; return true;
+        case GQ_TYPE_Q5_1: *ti = {32, 24, 32, true}; return true;
+        case GQ_TYPE_Q2_K: *ti = {256, 84, 16, true}; return true;
+        case GQ_TYPE_Q3_K: *ti = {256, 110, 16, false}; return true;
         default: return false;
     }
 }
@@ -102,8 +107,9 @@ gq::GqDesc make_desc(const gq_tensor_t& t, const TypeInfo& ti, int64_t n_units) 
 
 // Launch one kernel per GGML type present (the tensors are already validated).
 int launch_grouped(const std::vector<std::pair<gq::GqDesc, int>>& items, int out_mask, void* stream) {
-    static const int kTypes[] = {GQ_TYPE_Q4_K, GQ_TYPE_Q6_K, GQ_TYPE_Q5_K, GQ_TYPE_Q8_0,
-                                 GQ_TYPE_Q4_0, GQ_TYPE_F32, GQ_TYPE_F16, GQ_TYPE_BF16};
+    static const int kTypes[] = {GQ_TYPE_Q4_K, GQ_TYPE_Q6_K, GQ_TYPE_Q5_K, GQ_TYPE_Q8_0, GQ_TYPE_Q4_0,
+                                 GQ_TYPE_Q4_1, GQ_TYPE_Q5_0, GQ_TYPE_Q5_1, GQ_TYPE_Q2_K, GQ_TYPE_Q3_K,
+                                 GQ_TYPE_F32, GQ_TYPE_F16, GQ_TYPE_BF16};
     std::unique_ptr<gq::GqBatch> b(new (std::nothrow) gq::GqBatch);
     if (!b) return GQ_ERR_NOMEM;
     for (int type : kTypes) {

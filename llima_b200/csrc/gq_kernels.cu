@@ -57,6 +57,11 @@ GQ_FMT(GQ_TYPE_Q5_K, 176, 8 * GQ_Q5K_GROUPS, GQ_K45_STAGES)
 GQ_FMT(GQ_TYPE_Q6_K, 210, 8, 3)   // 128 blocks of 16 per tile
 GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4)   // 32 blocks of 32 per tile
 GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4)
+GQ_FMT(GQ_TYPE_Q4_1, 20, 32, 4)   // 32 blocks of 32 per tile, one per lane
+GQ_FMT(GQ_TYPE_Q5_0, 22, 32, 4)
+GQ_FMT(GQ_TYPE_Q5_1, 24, 32, 4)
+GQ_FMT(GQ_TYPE_Q2_K, 84, 8, 4)    // 128 blocks of 16 per tile, one per lane and round
+GQ_FMT(GQ_TYPE_Q3_K, 110, 8, 4)
 #undef GQ_FMT
 
 // Minimum resident CTAs per SM the Q4_K kernel is compiled for (caps its registers; the
@@ -465,6 +470,192 @@ __device__ __forceinline__ void process_q0(const GqDesc& D, int64_t unit0, int n
 }
 
 // ---------------------------------------------------------------------------------------
+// Q4_1 / Q5_0 / Q5_1 (ggml_quant.py:174-271; gguf_conversion.py:149-161) and the 16-value
+// K-quants Q2_K / Q3_K (ggml_quant.py:398-498, 587-623): one lane per output block, which
+// decodes, requantizes where the format is asymmetric, and stores its codes.
+// ---------------------------------------------------------------------------------------
+
+// 32 bits from a 2-byte-aligned shared address
+__device__ __forceinline__ uint32_t lds32_align2(const uint8_t* p) { return lds16(p) | (lds16(p + 2) << 16); }
+
+// 4 bits b0..b3 -> bit 4 of bytes 0..3 (the fifth bit of four 5-bit codes)
+__device__ __forceinline__ uint32_t spread_bits4(uint32_t b) { return ((b * 0x00204081u) & 0x01010101u) << 4; }
+
+// Codes of one block with requantization parameters p (any scale factor, with clipping).
+__device__ __forceinline__ uint32_t requant_word(uint32_t q4, const Requant& p) {
+    if (p.fast && !p.clip) {
+        const uint32_t k2 = static_cast<uint32_t>(p.rm + static_cast<int>(kLaneBias)) * 0x00010001u;
+        return requant_word_fast(q4, static_cast<uint32_t>(p.sfi), k2, false, 0u, 0u);
+    }
+    return requant_word_general(q4, p);
+}
+
+__device__ __forceinline__ void minmax_words(const uint32_t* q, int n, int& qmin, int& qmax) {
+    uint32_t mn = 0xFFFFFFFFu, mx = 0u;
+    for (int i = 0; i < n; ++i) {
+        mn = vmin16(vmin16(mn, q[i] & 0x00FF00FFu), (q[i] >> 8) & 0x00FF00FFu);
+        mx = vmax16(vmax16(mx, q[i] & 0x00FF00FFu), (q[i] >> 8) & 0x00FF00FFu);
+    }
+    qmin = min(mn & 0xFFFF, mn >> 16);
+    qmax = max(mx & 0xFFFF, mx >> 16);
+}
+
+template <int TYPE, int MODE>
+__device__ __forceinline__ void process_q32(const GqDesc& D, int64_t unit0, int nunits, const uint8_t* tile,
+                                            int lane, DiagAcc& acc, const float* recip) {
+    constexpr bool kQ5 = TYPE != GQ_TYPE_Q4_1;
+    constexpr bool kAsym = TYPE != GQ_TYPE_Q5_0;
+    constexpr int UB = Fmt<TYPE>::kUnitBytes;
+    constexpr int QH = TYPE == GQ_TYPE_Q5_0 ? 2 : 4;               // offset of qh (Q5_x)
+    constexpr int QS = TYPE == GQ_TYPE_Q4_1 ? 4 : (TYPE == GQ_TYPE_Q5_0 ? 6 : 8);
+    const bool valid = lane < nunits;
+    const uint8_t* bp = tile + UB * lane;
+    const float d = h2f(lds16(bp));
+    const float m = kAsym ? h2f(lds16(bp + 2)) : 0.0f;
+    const uint32_t qh = kQ5 ? lds32_align2(bp + QH) : 0u;
+    const uint4 nb = lds128_align2(bp + QS);
+    const uint32_t nw[4] = {nb.x, nb.y, nb.z, nb.w};
+    uint32_t q[8];   // values 0..15: low nibbles of bytes 0..15; 16..31: high nibbles
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        q[i] = nw[i] & 0x0F0F0F0Fu;
+        q[4 + i] = (nw[i] >> 4) & 0x0F0F0F0Fu;
+        if (kQ5) {
+            q[i] |= spread_bits4((qh >> (4 * i)) & 0xFu);
+            q[4 + i] |= spread_bits4((qh >> (16 + 4 * i)) & 0xFu);
+        }
+    }
+    const int64_t ou = permute_unit(D, unit0 + lane);
+    if (MODE & kOutCodes) {
+        uint32_t c[8];
+        float scale;
+        if (kAsym) {
+            // requantize_symmetric on the raw constants [d, m] (gguf_conversion.py:155-161)
+            int qmin, qmax;
+            minmax_words(q, 8, qmin, qmax);
+            const Requant p = requant_block(d, m, qmin, qmax, -128, 127, recip);
+            scale = p.scale;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) c[i] = requant_word(q[i], p);
+            if (valid) acc.add(p.round_err, p.clip_err);
+        } else {
+            // Q5_0: codes v - 16 as int8, per byte (v <= 31): (v + 0x70) ^ 0x80
+            scale = d;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) c[i] = (q[i] + 0x70707070u) ^ 0x80808080u;
+        }
+        if (valid) {
+            D.scales[ou] = scale;
+            stg128(D.codes + ou * 32, make_uint4(c[0], c[1], c[2], c[3]));
+            stg128(D.codes + ou * 32 + 16, make_uint4(c[4], c[5], c[6], c[7]));
+        }
+    }
+    if ((MODE & kOutF32) && valid) {
+        // gguf-py: Q4_1 / Q5_1 (d * q) + m, Q5_0 d * (q - 16)
+        float* dst = D.values + ou * 32;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float v[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int qv = static_cast<int>(byte_of(q[i], b));
+                v[b] = kAsym ? __fadd_rn(__fmul_rn(d, static_cast<float>(qv)), m)
+                             : __fmul_rn(d, static_cast<float>(qv - 16));
+            }
+            stg128f(dst + 4 * i, v[0], v[1], v[2], v[3]);
+        }
+    }
+}
+
+template <int TYPE, int MODE>
+__device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int nunits, const uint8_t* tile,
+                                            int lane, DiagAcc& acc, const float* recip) {
+    constexpr bool kQ2 = TYPE == GQ_TYPE_Q2_K;
+    constexpr int UB = Fmt<TYPE>::kUnitBytes;
+#pragma unroll 1
+    for (int r = 0; r < 4; ++r) {
+        const int c = 32 * r + lane;      // block of 16 values within the tile
+        const int sb = c >> 4;
+        const bool valid = sb < nunits;
+        const int kb = c & 15;
+        const uint8_t* sbp = tile + sb * UB;
+        const int h = kb >> 3, j = (kb >> 1) & 3, b0 = 16 * (kb & 1);
+        uint32_t q[4];
+        float d, dmin = 0.0f;
+        int sc, mn = 0;
+        if (kQ2) {
+            // scales[16] | qs[64] | d | dmin; value 128h + 32j + b = bits 2j..2j+1 of qs[32h + b]
+            const uint32_t sbyte = tile[sb * UB + kb];
+            sc = sbyte & 0xF;
+            mn = sbyte >> 4;
+            d = h2f(lds16(sbp + 80));
+            dmin = h2f(lds16(sbp + 82));
+            const uint4 x = lds128_align2(sbp + 16 + 32 * h + b0);
+            const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) q[i] = (xw[i] >> (2 * j)) & 0x03030303u;
+        } else {
+            // hmask[32] | qs[64] | scales[12] | d; third bit = bit 4h + j of hmask[b]; scale
+            // kb: low 4 bits from byte kb (low nibble) or kb - 8 (high nibble), top 2 bits
+            // from bits 2(kb/4).. of byte 8 + kb % 4, minus 32
+            const uint8_t* sp = sbp + 96;
+            const int low = kb < 8 ? (sp[kb] & 0xF) : (sp[kb - 8] >> 4);
+            const int top = (sp[8 + (kb & 3)] >> (2 * (kb >> 2))) & 3;
+            sc = (low | (top << 4)) - 32;
+            d = h2f(lds16(sbp + 108));
+            const uint4 x = lds128_align2(sbp + 32 + 32 * h + b0);
+            const uint4 hm = lds128_align2(sbp + b0);
+            const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+            const uint32_t hw[4] = {hm.x, hm.y, hm.z, hm.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                q[i] = ((xw[i] >> (2 * j)) & 0x03030303u) | (((hw[i] >> (4 * h + j)) & 0x01010101u) << 2);
+        }
+        const int64_t ou = permute_unit(D, unit0 + sb);
+        if (MODE & kOutCodes) {
+            // block constants f16(f32 product), min negated (ggml_quant.py:771-777)
+            const float S = round_to_f16(__fmul_rn(static_cast<float>(sc), d));
+            uint32_t cw[4];
+            if (kQ2) {
+                const float M = -round_to_f16(__fmul_rn(static_cast<float>(mn), dmin));
+                int qmin, qmax;
+                minmax_words(q, 4, qmin, qmax);
+                const Requant p = requant_block(S, M, qmin, qmax, -128, 127, recip);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) cw[i] = requant_word(q[i], p);
+                if (valid) {
+                    acc.add(p.round_err, p.clip_err);
+                    D.scales[ou * 16 + kb] = p.scale;
+                }
+            } else {
+                // Q3_K: codes q - 4 (per byte, q <= 7: (q + 0x7C) ^ 0x80), scale f16(sc * d)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) cw[i] = (q[i] + 0x7C7C7C7Cu) ^ 0x80808080u;
+                if (valid) D.scales[ou * 16 + kb] = S;
+            }
+            if (valid) stg128(D.codes + ou * 256 + 16 * kb, make_uint4(cw[0], cw[1], cw[2], cw[3]));
+        }
+        if ((MODE & kOutF32) && valid) {
+            // gguf-py: Q2_K (d*sc)*q - dmin*m; Q3_K (d*sc)*(q - 4)
+            const float dl = __fmul_rn(d, static_cast<float>(sc));
+            const float ml = __fmul_rn(dmin, static_cast<float>(mn));
+            float* dst = D.values + ou * 256 + 16 * kb;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float v[4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int qv = static_cast<int>(byte_of(q[i], b));
+                    v[b] = kQ2 ? __fsub_rn(__fmul_rn(dl, static_cast<float>(qv)), ml)
+                               : __fmul_rn(dl, static_cast<float>(qv - 4));
+                }
+                stg128f(dst + 4 * i, v[0], v[1], v[2], v[3]);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
 // The persistent per-warp pipeline shared by all block formats
 // ---------------------------------------------------------------------------------------
 
@@ -514,6 +705,12 @@ __global__ void __launch_bounds__(kThreads, TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS
                 D, unit0, nunits, tile, lane, acc, recip);
         } else if (TYPE == GQ_TYPE_Q6_K) {
             process_q6k<MODE>(D, unit0, nunits, tile, lane);
+        } else if (TYPE == GQ_TYPE_Q4_1 || TYPE == GQ_TYPE_Q5_0 || TYPE == GQ_TYPE_Q5_1) {
+            if (MODE & kOutCodes) acc.retarget(D.diag, lane);
+            process_q32<TYPE, MODE>(D, unit0, nunits, tile, lane, acc, recip);
+        } else if (TYPE == GQ_TYPE_Q2_K || TYPE == GQ_TYPE_Q3_K) {
+            if (MODE & kOutCodes) acc.retarget(D.diag, lane);
+            process_k16<TYPE, MODE>(D, unit0, nunits, tile, lane, acc, recip);
         } else {
             process_q0<TYPE == GQ_TYPE_Q4_0, MODE>(D, unit0, nunits, tile, lane);
         }
@@ -521,7 +718,10 @@ __global__ void __launch_bounds__(kThreads, TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS
         stage = (stage + 1 == F::kStages) ? 0 : stage + 1;
     }
     cp_async_wait<0>();
-    if ((TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K) && (MODE & kOutCodes)) acc.flush(lane);
+    if ((MODE & kOutCodes) && (TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K || TYPE == GQ_TYPE_Q4_1 ||
+                               TYPE == GQ_TYPE_Q5_0 || TYPE == GQ_TYPE_Q5_1 || TYPE == GQ_TYPE_Q2_K ||
+                               TYPE == GQ_TYPE_Q3_K))
+        acc.flush(lane);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -672,6 +872,11 @@ int64_t tiles_for(int type, int64_t n_units) {
         case GQ_TYPE_Q6_K: upt = Fmt<GQ_TYPE_Q6_K>::kUnitsPerTile; break;
         case GQ_TYPE_Q8_0: upt = Fmt<GQ_TYPE_Q8_0>::kUnitsPerTile; break;
         case GQ_TYPE_Q4_0: upt = Fmt<GQ_TYPE_Q4_0>::kUnitsPerTile; break;
+        case GQ_TYPE_Q4_1: upt = Fmt<GQ_TYPE_Q4_1>::kUnitsPerTile; break;
+        case GQ_TYPE_Q5_0: upt = Fmt<GQ_TYPE_Q5_0>::kUnitsPerTile; break;
+        case GQ_TYPE_Q5_1: upt = Fmt<GQ_TYPE_Q5_1>::kUnitsPerTile; break;
+        case GQ_TYPE_Q2_K: upt = Fmt<GQ_TYPE_Q2_K>::kUnitsPerTile; break;
+        case GQ_TYPE_Q3_K: upt = Fmt<GQ_TYPE_Q3_K>::kUnitsPerTile; break;
         case GQ_TYPE_F32: upt = kCopyTileBytes / 4; break;
         default: upt = kCopyTileBytes / 2; break;   // F16, BF16
     }
@@ -686,6 +891,11 @@ int launch_batch(int type, int out_mask, const GqBatch& b, void* stream) {
         case GQ_TYPE_Q6_K: return launch_modes<GQ_TYPE_Q6_K>(out_mask, b, s);
         case GQ_TYPE_Q8_0: return launch_modes<GQ_TYPE_Q8_0>(out_mask, b, s);
         case GQ_TYPE_Q4_0: return launch_modes<GQ_TYPE_Q4_0>(out_mask, b, s);
+        case GQ_TYPE_Q4_1: return launch_modes<GQ_TYPE_Q4_1>(out_mask, b, s);
+        case GQ_TYPE_Q5_0: return launch_modes<GQ_TYPE_Q5_0>(out_mask, b, s);
+        case GQ_TYPE_Q5_1: return launch_modes<GQ_TYPE_Q5_1>(out_mask, b, s);
+        case GQ_TYPE_Q2_K: return launch_modes<GQ_TYPE_Q2_K>(out_mask, b, s);
+        case GQ_TYPE_Q3_K: return launch_modes<GQ_TYPE_Q3_K>(out_mask, b, s);
         case GQ_TYPE_F32: return launch_copy<4>(b, s);
         default: return launch_copy<2>(b, s);
     }

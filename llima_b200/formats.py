@@ -30,6 +30,11 @@ FORMATS: dict[str, Format] = {
     "Q4_K": Format("Q4_K", 12, 256, 144, 32, True),
     "Q5_K": Format("Q5_K", 13, 256, 176, 32, True),
     "Q6_K": Format("Q6_K", 14, 256, 210, 16, False),
+    "Q4_1": Format("Q4_1", 3, 32, 20, 32, True),
+    "Q5_0": Format("Q5_0", 6, 32, 22, 32, False),
+    "Q5_1": Format("Q5_1", 7, 32, 24, 32, True),
+    "Q2_K": Format("Q2_K", 10, 256, 84, 16, True),
+    "Q3_K": Format("Q3_K", 11, 256, 110, 16, False),
 }
 FORMAT_BY_ID = {f.type_id: f for f in FORMATS.values()}
 

@@ -6,7 +6,8 @@ quantized types ``(scales f32 (n_blocks, 1), codes (rows, cols))`` with int8 cod
 ml_dtypes int4 for Q4_0), for ``force_float=True`` ``(None, f32 (rows, cols))`` as
 gguf-py's ``dequantize`` computes it, and float tensors unchanged.  The decode runs in
 libgguf_b200.so through ``gq_convert_host``; there is no CPU fallback: a type outside
-the path (Q4_1, Q5_0, Q5_1, Q8_1, Q2_K, Q3_K, IQ*) raises ``NotImplementedError``.
+the path (IQ*, TQ*, MXFP4 ...) raises ``NotImplementedError``, and Q8_1 raises the
+``KeyError`` the reference's format table raises for it (``ggml_quant.py:716``).
 
 ``GgufReaderProxy`` mirrors the reference class (``gguf_conversion.py:179-205``), and
 ``install`` swaps this decode (and the fused q/k head permutation) into an imported
@@ -32,7 +33,7 @@ __all__ = ["unpack_gguf_tensor", "load_tensor", "convert_host", "GgufReaderProxy
 # Same logger and text as ggml_quant.py:879-880, so log handling stays as it was.
 _log = logging.getLogger("sima_lmm.gguf.ggml_quant")
 
-_GPU_TYPES = {"Q8_0", "Q4_0", "Q4_K", "Q5_K", "Q6_K"}
+_GPU_TYPES = {"Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"}
 _sessions: dict[tuple[int, int], ctypes.c_void_p] = {}
 _sessions_lock = threading.Lock()
 
@@ -142,6 +143,8 @@ def load_tensor(gguf_tensor, force_float: bool, perm_heads: int = 0):
             rows = shape[0]
             w = w.reshape(perm_heads, rows // perm_heads // 2, 2, *shape[1:]).swapaxes(1, 2).reshape(shape)
         return None, w
+    if name == "Q8_1" and not force_float:
+        raise KeyError("Q8_1")
     if name not in _GPU_TYPES:
         raise NotImplementedError(f"GGML type {name} is not handled by the B200 GGUF path")
     rows = shape[0]

@@ -83,6 +83,16 @@ def gen_tensor_bytes(fmt: str, n_values: int, seed: int, kind: str = "weight") -
     elif fmt == "Q6_K":
         u[:, 192:208] = rng.integers(-64, 64, size=(n, 16), dtype=np.int8).view(np.uint8)
         u[:, 208:210] = _f16_uniform(rng, n)
+    elif fmt in ("Q4_1", "Q5_1"):
+        u[:, 0:2] = _f16_uniform(rng, n)
+        u[:, 2:4] = _f16_uniform(rng, n, -0.15, 0.0)    # the block minimum
+    elif fmt == "Q5_0":
+        u[:, 0:2] = _f16_uniform(rng, n)
+    elif fmt == "Q2_K":
+        u[:, 80:82] = _f16_uniform(rng, n)
+        u[:, 82:84] = _f16_uniform(rng, n)
+    elif fmt == "Q3_K":
+        u[:, 108:110] = _f16_uniform(rng, n)
     else:
         raise ValueError(f"unsupported synthetic format {fmt}")
     return u.reshape(-1)

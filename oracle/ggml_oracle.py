@@ -62,6 +62,11 @@ FORMATS: dict[str, Format] = {
     "Q4_K": Format("Q4_K", 12, 256, 144, 32, 2),
     "Q5_K": Format("Q5_K", 13, 256, 176, 32, 2),
     "Q6_K": Format("Q6_K", 14, 256, 210, 16, 1),
+    "Q4_1": Format("Q4_1", 3, 32, 20, 32, 2),
+    "Q5_0": Format("Q5_0", 6, 32, 22, 32, 1),
+    "Q5_1": Format("Q5_1", 7, 32, 24, 32, 2),
+    "Q2_K": Format("Q2_K", 10, 256, 84, 16, 2),
+    "Q3_K": Format("Q3_K", 11, 256, 110, 16, 1),
 }
 FORMAT_BY_ID = {f.type_id: f for f in FORMATS.values()}
 
@@ -101,6 +106,36 @@ def unpack_q4_0(data) -> tuple[np.ndarray, np.ndarray]:
     vals[:, :16] = (body & 0x0F).astype(np.int8) - 8
     vals[:, 16:] = (body >> 4).astype(np.int8) - 8
     return scales, vals.astype(int4)
+
+
+def _q5_values(u: np.ndarray, qh_off: int) -> np.ndarray:
+    """Q5_0/Q5_1 values 0..31: value j takes the low (j < 16) or high (j >= 16) nibble of
+    byte j % 16 and bit j of the little-endian uint32 at qh_off.  ``ggml_quant.py:230-271``."""
+    qh = np.ascontiguousarray(u[:, qh_off:qh_off + 4]).view(np.uint32)[:, 0]
+    body = u[:, qh_off + 4:qh_off + 20]
+    nib = np.concatenate([body & 0x0F, body >> 4], axis=1).astype(np.uint8)
+    bits = ((qh[:, None] >> np.arange(32, dtype=np.uint32)[None, :]) & 1).astype(np.uint8)
+    return (nib | (bits << 4)).astype(np.int8)
+
+
+def unpack_q5_0(data) -> tuple[np.ndarray, np.ndarray]:
+    """Q5_0 symmetric: scale f32(d), codes q - 16 as int8.  ``ggml_quant.py:230-271`` via
+    ``gguf_conversion.py:149-153``."""
+    u = _units(data, FORMATS["Q5_0"])
+    return _f16_field(u, 0).reshape(-1, 1), _q5_values(u, 2) - np.int8(16)
+
+
+def unpack_asym_base(data, name: str):
+    """Q4_1 / Q5_1: constants [d, m] f32 (not negated) and unsigned codes, as
+    ``unpack_base_quant`` returns them (``ggml_quant.py:706-736``)."""
+    u = _units(data, FORMATS[name])
+    consts = np.stack([_f16_field(u, 0), _f16_field(u, 2)], axis=1)
+    if name == "Q4_1":
+        body = u[:, 4:20]
+        q = np.concatenate([body & 0x0F, body >> 4], axis=1).astype(np.int8)
+    else:
+        q = _q5_values(u, 4)
+    return consts, q
 
 
 # ---------------------------------------------------------------------------
@@ -168,6 +203,32 @@ def _q6_k_values(ql: np.ndarray, qh: np.ndarray) -> np.ndarray:
     return (out.view(np.int8) - np.int8(32)).reshape(n, 16, 16)
 
 
+def _q2_k_values(qs: np.ndarray) -> np.ndarray:
+    """Q2_K: bit pair j of byte b of half h is value 128h + 32j + b.  ``ggml_quant.py:479-498``."""
+    halves = qs.reshape(-1, 2, 1, 32)
+    out = (halves >> np.array([0, 2, 4, 6], dtype=np.uint8).reshape(1, 1, 4, 1)) & 3
+    return out.astype(np.int8).reshape(-1, 16, 16)
+
+
+def _q3_k_values(hmask: np.ndarray, qs: np.ndarray) -> np.ndarray:
+    """Q3_K: low 2 bits as Q2_K, third bit = bit 4h + j of hmask[b], minus 4.
+    ``ggml_quant.py:428-463``."""
+    low = (qs.reshape(-1, 2, 1, 32) >> np.array([0, 2, 4, 6], dtype=np.uint8).reshape(1, 1, 4, 1)) & 3
+    hb = (hmask.reshape(-1, 1, 1, 32) >> np.arange(8, dtype=np.uint8).reshape(1, 2, 4, 1)) & 1
+    return ((low | (hb << 2)).astype(np.int8) - np.int8(4)).reshape(-1, 16, 16)
+
+
+def _q3_k_scales(b: np.ndarray) -> np.ndarray:
+    """Q3_K: 16 six-bit scales minus 32.  Scale i: low 4 bits from byte i (i < 8, low
+    nibble) or byte i - 8 (high nibble), top 2 bits = bits 2(i//4)..+1 of byte 8 + i % 4.
+    ``ggml_quant.py:398-425``."""
+    b = b.astype(np.uint8)
+    i = np.arange(16)
+    low = np.where(i < 8, b[:, i % 8] & 0x0F, b[:, i % 8] >> 4)
+    top = (b[:, 8 + i % 4] >> (2 * (i // 4)).astype(np.uint8)) & 3
+    return ((low | (top << 4)).astype(np.int8) - np.int8(32)).reshape(-1, 16, 1)
+
+
 def unpack_k_quant(data, name: str) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
     """Split K-quant super-blocks into (super constants f32 (N,k), block constants
     int8 (N,B,k), values int8 (N,B,C)).  ``ggml_quant.py:567-694``; field order per
@@ -184,6 +245,14 @@ def unpack_k_quant(data, name: str) -> tuple[np.ndarray, np.ndarray, np.ndarray]
         sc, mn = unpack_6bit_scale_min(u[:, 4:16])
         blk = np.stack([sc, mn], axis=2)
         vals = _q5_k_values(u[:, 16:48], u[:, 48:176])
+    elif name == "Q2_K":    # scales[16] (4-bit scale | 4-bit min << 4) | qs[64] | d, dmin
+        sup = np.stack([_f16_field(u, 80), _f16_field(u, 82)], axis=1)
+        blk = np.stack([(u[:, 0:16] & 0x0F).astype(np.int8), (u[:, 0:16] >> 4).astype(np.int8)], axis=2)
+        vals = _q2_k_values(u[:, 16:80])
+    elif name == "Q3_K":    # hmask[32] | qs[64] | scales[12] | d
+        sup = _f16_field(u, 108).reshape(-1, 1)
+        blk = _q3_k_scales(u[:, 96:108])
+        vals = _q3_k_values(u[:, 0:32], u[:, 32:96])
     elif name == "Q6_K":    # ql[128] | qh[64] | scales int8[16] | d
         sup = _f16_field(u, 208).reshape(-1, 1)
         blk = np.ascontiguousarray(u[:, 192:208]).view(np.int8).reshape(-1, 16, 1)
@@ -305,6 +374,25 @@ def gguf_dequantize(data, name: str) -> np.ndarray:
         else:
             q = _q5_k_values(u[:, 16:48], u[:, 48:176])
         return (ds * q.astype(np.float32) - dm).reshape(-1)
+    if name == "Q4_1":      # (d * q) + m
+        consts, q = unpack_asym_base(data, name)
+        return (consts[:, :1] * q.astype(np.float32) + consts[:, 1:2]).reshape(-1)
+    if name == "Q5_1":      # (d * q) + m
+        consts, q = unpack_asym_base(data, name)
+        return (consts[:, :1] * q.astype(np.float32) + consts[:, 1:2]).reshape(-1)
+    if name == "Q5_0":      # d * (q - 16)
+        d = _f16_field(u, 0)[:, None]
+        return (d * (_q5_values(u, 2) - np.int8(16)).astype(np.float32)).reshape(-1)
+    if name == "Q2_K":      # (d*sc)*q - dmin*m
+        d = _f16_field(u, 80)[:, None]
+        dmin = _f16_field(u, 82)[:, None]
+        dl = (d * (u[:, 0:16] & 0x0F).astype(np.float32))[:, :, None]
+        ml = (dmin * (u[:, 0:16] >> 4).astype(np.float32))[:, :, None]
+        return (dl * _q2_k_values(u[:, 16:80]).astype(np.float32) - ml).reshape(-1)
+    if name == "Q3_K":      # (d*sc) * q
+        d = _f16_field(u, 108)[:, None]
+        dl = (d * _q3_k_scales(u[:, 96:108])[:, :, 0].astype(np.float32))[:, :, None]
+        return (dl * _q3_k_values(u[:, 0:32], u[:, 32:96]).astype(np.float32)).reshape(-1)
     if name == "Q6_K":      # (d*sc) * q
         d = _f16_field(u, 208)
         sc = np.ascontiguousarray(u[:, 192:208]).view(np.int8).astype(np.float32)
@@ -350,7 +438,12 @@ def unpack_tensor(name: str, data, shape_rows_cols: tuple[int, ...], force_float
         s, w = unpack_q8_0(data)
     elif name == "Q4_0":
         s, w = unpack_q4_0(data)
-    elif name in ("Q4_K", "Q5_K", "Q6_K"):
+    elif name == "Q5_0":
+        s, w = unpack_q5_0(data)
+    elif name in ("Q4_1", "Q5_1"):
+        consts, q = unpack_asym_base(data, name)
+        s, w, diag = requantize_symmetric(consts, q, 8, np.int8, log=log)
+    elif name in ("Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"):
         s, w, diag = convert_k_quant(data, name, log=log)
     else:
         raise NotImplementedError(name)

@@ -148,7 +148,10 @@ def main():
 
     shapes = {"Q8_0": [(37, 64), (6, 4096)], "Q4_0": [(37, 64), (6, 4096)],
               "Q4_K": [(37, 256), (5, 4096)], "Q5_K": [(37, 256), (5, 4096)],
-              "Q6_K": [(37, 256), (5, 4096)]}
+              "Q6_K": [(37, 256), (5, 4096)],
+              "Q4_1": [(37, 64), (6, 1024)], "Q5_0": [(37, 64), (6, 1024)],
+              "Q5_1": [(37, 64), (6, 1024)], "Q2_K": [(37, 256), (3, 2048)],
+              "Q3_K": [(37, 256), (3, 2048)]}
     for fmt, shp in shapes.items():
         for seed in (0, 1, 2):
             for rows, cols in shp:
@@ -160,6 +163,7 @@ def main():
             12 if FORMATS[fmt].unit_values == 256 else 48, 2048 if FORMATS[fmt].unit_values == 256 else 256)
     for fmt in ("Q4_K", "Q5_K", "Q6_K"):
         run(f"{fmt}_edges", fmt, _edge_kquant(fmt, 96, 11), 24, 1024)
+    run("Q2_K_perm_q", "Q2_K", gen_tensor_bytes("Q2_K", 32 * 512, 25), 32, 512, heads=2)
     # q/k head permutation of a llama-style model: 4 heads of dim 16, and 2 kv heads
     run("Q4_K_perm_q", "Q4_K", gen_tensor_bytes("Q4_K", 64 * 512, 21), 64, 512, heads=4)
     run("Q6_K_perm_k", "Q6_K", gen_tensor_bytes("Q6_K", 32 * 512, 22), 32, 512, heads=2)

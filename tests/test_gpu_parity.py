@@ -70,7 +70,8 @@ def test_golden(case):
 
 # BASELINE configs 1 and 2 at full size, plus the other two K formats at the same shape
 FULL = [("Q8_0", 4096, 4096), ("Q4_0", 11008, 4096), ("Q4_K", 11008, 4096),
-        ("Q5_K", 11008, 4096), ("Q6_K", 11008, 4096)]
+        ("Q5_K", 11008, 4096), ("Q6_K", 11008, 4096), ("Q4_1", 4096, 4096), ("Q5_0", 4096, 4096),
+        ("Q5_1", 4096, 4096), ("Q2_K", 4096, 4096), ("Q3_K", 4096, 4096)]
 
 
 @pytest.mark.parametrize("fmt,rows,cols", FULL, ids=[f[0] for f in FULL])
@@ -89,7 +90,7 @@ def test_full_size_vs_oracle(fmt, rows, cols):
         assert same_bits(np.float32(r), np.float32(d.round_error)) and int(c) == int(d.clip_error)
 
 
-@pytest.mark.parametrize("fmt", ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0"])
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K"])
 @pytest.mark.parametrize("mask", [N.OUT_CODES, N.OUT_F32])
 def test_single_output_modes_match_both(fmt, mask):
     rows, cols = 64, 2048
@@ -105,7 +106,7 @@ def test_single_output_modes_match_both(fmt, mask):
         assert one.codes is None
 
 
-@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K", "Q8_0"])
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K", "Q8_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K"])
 def test_uniform_random_bytes_vs_oracle(fmt):
     # every f16 field random: NaN, inf, subnormal and huge constants
     f = FORMATS[fmt]
@@ -257,7 +258,7 @@ def test_invalid_arguments_return_errors_without_launch():
     t.perm_heads = 3                                # rows not divisible by 2*heads
     assert lib.gq_convert(ctypes.byref(t), N.OUT_CODES, None) == -5
     t.perm_heads = 0
-    t.type = 3                                      # Q4_1: not on this path
+    t.type = 9                                      # Q8_1: not on this path
     assert lib.gq_convert(ctypes.byref(t), N.OUT_CODES, None) == -1
     t.type, t.rows = 12, 0                          # empty tensor: nothing to do
     assert lib.gq_convert(ctypes.byref(t), N.OUT_CODES, None) == 0
