@@ -143,6 +143,23 @@ GQ_API int gq_requantize_symmetric(const float* block_consts, const int8_t* code
                             int32_t block, int32_t output_bits, float* out_scales,
                             int8_t* out_codes, gq_diag_t* diag, void* stream);
 
+/* Token embeddings for the on-device runtime: LanguageModel.get_embeddings_tensor
+ * (sima_lmm/model/language_model.py:578-611) fused with quantize_embedding_rows (:38-54).
+ * Each row of a GGUF tensor (type F32, F16, BF16, Q8_0, Q4_0, Q4_K, Q5_K or Q6_K; src in
+ * device memory, 16-byte aligned) is dequantized as gguf-py does, multiplied by
+ * embed_scale (f32) and rounded to bf16.  quantize != 0: int8 codes (rows x cols) and one
+ * bf16 scale per row (the row's absmax; 0 for an all-zero row); quantize == 0: the
+ * bf16-rounded values as f32 (rows x cols).  cols must be a multiple of 4 and of the
+ * type's block, and one row at most 51168 GGUF bytes. */
+GQ_API int gq_embedding_rows(int32_t type, const void* src, size_t src_bytes, int64_t rows, int64_t cols,
+                             float embed_scale, int32_t quantize, int8_t* codes, uint16_t* scales_bf16,
+                             float* values, void* stream);
+
+/* quantize_embedding_rows (language_model.py:38-54) on f32 rows in device memory:
+ * int8 codes (rows x cols) and bf16 absmax scales (rows). */
+GQ_API int gq_quantize_rows(const float* x, int64_t rows, int64_t cols, int8_t* codes, uint16_t* scales_bf16,
+                            void* stream);
+
 /* Host-buffer path: an opaque per-device session owning device staging memory and
  * streams.  gq_convert_host copies each tensor's bytes host->device, converts and copies
  * the results device->host, pipelining tensors (and pieces of large tensors) across two

@@ -240,6 +240,47 @@ int gq_requantize_symmetric(const float* block_consts, const int8_t* codes, int6
                                           out_codes, diag, stream));
 }
 
+int gq_embedding_rows(int32_t type, const void* src, size_t src_bytes, int64_t rows, int64_t cols,
+                      float embed_scale, int32_t quantize, int8_t* codes, uint16_t* scales_bf16, float* values,
+                      void* stream) {
+    TypeInfo ti;
+    if (!type_info(type, &ti)) return GQ_ERR_TYPE;
+    switch (type) {   // the formats token embeddings come in
+        case GQ_TYPE_F32: case GQ_TYPE_F16: case GQ_TYPE_BF16: case GQ_TYPE_Q8_0: case GQ_TYPE_Q4_0:
+        case GQ_TYPE_Q4_K: case GQ_TYPE_Q5_K: case GQ_TYPE_Q6_K: break;
+        default: return GQ_ERR_TYPE;
+    }
+    if (rows < 0 || cols < 0 || cols % ti.unit_values != 0 || cols % 4 != 0) return GQ_ERR_SIZE;
+    const int64_t row_bytes = cols / ti.unit_values * ti.unit_bytes;
+    if (row_bytes > gq::embed_max_row_bytes()) return GQ_ERR_SIZE;
+    if (cols != 0 && rows > INT64_MAX / cols) return GQ_ERR_SIZE;
+    if (static_cast<uint64_t>(rows * row_bytes) > src_bytes) return GQ_ERR_SIZE;
+    if (rows == 0 || cols == 0) return GQ_OK;
+    if (src == nullptr) return GQ_ERR_NULL;
+    if (!aligned(src, 16)) return GQ_ERR_ALIGN;
+    if (quantize) {
+        if (codes == nullptr || scales_bf16 == nullptr) return GQ_ERR_NULL;
+        if (!aligned(codes, 4) || !aligned(scales_bf16, 2)) return GQ_ERR_ALIGN;
+    } else {
+        if (values == nullptr) return GQ_ERR_NULL;
+        if (!aligned(values, 16)) return GQ_ERR_ALIGN;
+    }
+    return cuda_status(gq::launch_embed(type, false, static_cast<const uint8_t*>(src), rows, cols, row_bytes,
+                                        embed_scale, quantize ? 1 : 0, codes, scales_bf16, values,
+                                        static_cast<int64_t>(src_bytes), stream));
+}
+
+int gq_quantize_rows(const float* x, int64_t rows, int64_t cols, int8_t* codes, uint16_t* scales_bf16,
+                     void* stream) {
+    if (rows < 0 || cols < 0 || cols % 4 != 0) return GQ_ERR_SIZE;
+    if (cols * 4 > gq::embed_max_row_bytes()) return GQ_ERR_SIZE;
+    if (rows == 0 || cols == 0) return GQ_OK;
+    if (x == nullptr || codes == nullptr || scales_bf16 == nullptr) return GQ_ERR_NULL;
+    if (!aligned(x, 16) || !aligned(codes, 4) || !aligned(scales_bf16, 2)) return GQ_ERR_ALIGN;
+    return cuda_status(gq::launch_embed(GQ_TYPE_F32, true, reinterpret_cast<const uint8_t*>(x), rows, cols, cols * 4,
+                                        1.0f, 1, codes, scales_bf16, nullptr, rows * cols * 4, stream));
+}
+
 // ---------------------------------------------------------------------------------------
 // Host-buffer session
 // ---------------------------------------------------------------------------------------
