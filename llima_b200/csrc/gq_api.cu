@@ -240,6 +240,20 @@ int gq_requantize_symmetric(const float* block_consts, const int8_t* codes, int6
                                           out_codes, diag, stream));
 }
 
+int gq_modalix_layout(const void* codes, const float* scales, int64_t rows, int64_t cols, int32_t block_values,
+                      int64_t rows_padded, void* out_codes, float* out_scales, void* stream) {
+    if (rows < 0 || cols < 0 || rows_padded < rows) return GQ_ERR_SIZE;
+    if (block_values <= 0 || cols % block_values != 0) return GQ_ERR_SIZE;
+    if (cols > (int64_t(65535) * 32) || rows_padded > INT32_MAX) return GQ_ERR_SIZE;
+    if (rows_padded == 0 || cols == 0) return GQ_OK;
+    if ((codes == nullptr) != (out_codes == nullptr) || (scales == nullptr) != (out_scales == nullptr))
+        return GQ_ERR_NULL;
+    if (codes == nullptr && scales == nullptr) return GQ_ERR_NULL;
+    if ((scales && !aligned(scales, 4)) || (out_scales && !aligned(out_scales, 4))) return GQ_ERR_ALIGN;
+    return cuda_status(gq::launch_layout(static_cast<const uint8_t*>(codes), scales, rows, cols, cols / block_values,
+                                         rows_padded, static_cast<uint8_t*>(out_codes), out_scales, stream));
+}
+
 int gq_embedding_rows(int32_t type, const void* src, size_t src_bytes, int64_t rows, int64_t cols,
                       float embed_scale, int32_t quantize, int8_t* codes, uint16_t* scales_bf16, float* values,
                       void* stream) {

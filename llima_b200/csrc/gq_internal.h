@@ -38,6 +38,8 @@ enum : int { kOutCodes = GQ_OUT_CODES, kOutF32 = GQ_OUT_F32 };
 // launch entry points implemented in gq_kernels.cu
 int launch_batch(int type, int out_mask, const GqBatch& batch, void* stream);
 int64_t tiles_for(int type, int64_t n_units);
+int launch_layout(const uint8_t* codes, const float* scales, int64_t rows, int64_t cols, int64_t nb,
+                  int64_t rows_padded, uint8_t* out_codes, float* out_scales, void* stream);
 int64_t embed_max_row_bytes();
 int launch_embed(int type, bool from_f32, const uint8_t* src, int64_t rows, int64_t cols, int64_t row_bytes,
                  float embed_scale, int quantize, int8_t* codes, uint16_t* scales, float* values, int64_t src_bytes,

@@ -472,3 +472,35 @@ def quantize_embedding_rows(emb: np.ndarray):
     scales = (step * np.float32(127.0)).astype(np.float32)
     scales[np.count_nonzero(x, axis=1) == 0] = 0.0
     return q, scales.reshape(-1, 1).astype(bfloat16)
+
+
+# ---------------------------------------------------------------------------
+# Modalix weight layout (ModelGraph._build_conv)
+# ---------------------------------------------------------------------------
+
+MLA_ROW_SIZE = 16   # sima_lmm/utils.py:4
+
+
+def padded_output_channels(out_channels: int, is_int4: bool, pad_output: bool = True) -> int:
+    """Output channels after the int4 32-way padding of ``model_graph.py:1057-1069`` (for a
+    non-relocatable, non-quantizable graph with scales)."""
+    split_width = ((-(-out_channels // MLA_ROW_SIZE) + 31) // 32) * MLA_ROW_SIZE
+    if (pad_output and is_int4 and out_channels > 512 and out_channels % MLA_ROW_SIZE == 0
+            and out_channels - 31 * split_width <= 0):
+        return 32 * split_width
+    return out_channels
+
+
+def modalix_layout(scales: np.ndarray, codes: np.ndarray, padded: int):
+    """``model_graph.py:1012-1079`` with the default oi->oihw reshape and no process
+    functions: scales (O*I/B, 1) -> (I/B, O'), codes (O, I) -> HWIGO (1, 1, I, 1, O'),
+    padded with zero codes and unit scales to O' output channels."""
+    out_ch = codes.shape[0]
+    s = np.transpose(np.reshape(scales, (out_ch, -1)), (1, 0))
+    # _layout_array(w, "oi", "oihw") then (w, "oihw", "hwigo") (model_graph.py:1271-1304)
+    w = np.transpose(np.expand_dims(codes.reshape(out_ch, -1, 1, 1), 0), (3, 4, 2, 0, 1))
+    extra = padded - out_ch
+    if extra:
+        w = np.pad(w, ((0, 0),) * 4 + ((0, extra),))
+        s = np.pad(s, ((0, 0), (0, extra)), constant_values=1)
+    return s, w

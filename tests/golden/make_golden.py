@@ -170,6 +170,26 @@ def main():
     run("Q8_0_perm_q", "Q8_0", gen_tensor_bytes("Q8_0", 64 * 128, 23), 64, 128, heads=4)
     run("F32_norm", "F32", gen_tensor_bytes("F32", 1000, 24, "norm"), 1000, 1)
 
+    # Modalix layout: the reference's own _layout_array (model_graph.py:1271-1304), taken
+    # from the source file (the module imports the absent afe SDK), applied as
+    # _build_conv does (model_graph.py:1012-1042)
+    import ast
+    src_path = Path(args.reference) / "sima_lmm" / "model" / "model_graph.py"
+    tree = ast.parse(src_path.read_text())
+    fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "_layout_array")
+    ns: dict = {"np": np}
+    exec(compile(ast.Module(body=[fn], type_ignores=[]), str(src_path), "exec"), ns)
+    layout_array = ns["_layout_array"]
+    for case, (out_ch, in_ch, block) in {"layout_97x96": (97, 96, 32), "layout_64x512": (64, 512, 16)}.items():
+        rng = np.random.default_rng(out_ch)
+        codes = rng.integers(-128, 128, size=(out_ch, in_ch), dtype=np.int8)
+        scales = rng.random((out_ch * in_ch // block, 1), dtype=np.float32)
+        sc = np.transpose(np.reshape(scales, (codes.shape[0], -1)), axes=[1, 0])
+        w = layout_array(layout_array(codes, "oi", "oihw"), "oihw", "hwigo")
+        np.savez_compressed(out / f"{case}.npz", codes=codes, scales=scales, out_scales=sc, out_weight=w,
+                            block=block, kind="layout")
+        manifest.append({"case": case, "fmt": "layout", "rows": out_ch, "cols": in_ch})
+
     versions = {"numpy": np.__version__, "ml_dtypes": ml_dtypes.__version__,
                 "gguf": getattr(gguf, "__version__", None) or _dist_version("gguf"),
                 "reference": "sima-neat/llima 0.6.2", "cases": manifest}

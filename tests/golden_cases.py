@@ -7,7 +7,12 @@ GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
 def case_names(prefix: str = "") -> list[str]:
-    return sorted(p.stem for p in GOLDEN.glob(f"{prefix}*.npz"))
+    """Golden cases of the GGUF conversion (the layout cases are listed by layout_cases)."""
+    return sorted(p.stem for p in GOLDEN.glob(f"{prefix}*.npz") if not p.stem.startswith("layout_"))
+
+
+def layout_cases() -> list[str]:
+    return sorted(p.stem for p in GOLDEN.glob("layout_*.npz"))
 
 
 def load_case(name: str) -> dict:

@@ -106,3 +106,14 @@ def test_i16_cast_follows_numpy_x86():
     with np.errstate(all="ignore"):
         want = x.astype(np.int16)
     assert np.array_equal(O._i16_cast(x), want)
+
+
+def test_layout_restatement_matches_reference_layout_array():
+    from tests.golden_cases import GOLDEN, layout_cases
+    cases = layout_cases()
+    assert cases
+    for name in cases:
+        with np.load(GOLDEN / f"{name}.npz") as z:
+            s, w = O.modalix_layout(z["scales"], z["codes"], z["codes"].shape[0])
+            assert s.shape == z["out_scales"].shape and np.array_equal(s, z["out_scales"])
+            assert w.shape == z["out_weight"].shape and np.array_equal(w, z["out_weight"])
