@@ -111,6 +111,58 @@ def _cpu_worker(model, seed, rank, sample_mb, seconds, passes, barrier, queue):
     queue.put((done, t0, time.time()))
 
 
+def _cpu_step_worker(model, seed, rank, sample_mb, n_steps, barrier, queue):
+    """One worker of the reference arm: n_steps synchronized passes over its sample."""
+    sys.path.insert(0, str(ROOT))
+    from llima_b200.synth import gen_tensor_bytes, model_specs
+    from oracle import ggml_oracle as O
+    specs = [s for s in model_specs(model, seed) if s.fmt != "F32"]
+    by_fmt: dict[str, int] = {}
+    for s in specs:
+        by_fmt[s.fmt] = by_fmt.get(s.fmt, 0) + s.nbytes
+    total = sum(by_fmt.values())
+    sample = []
+    for fmt, nb in sorted(by_fmt.items()):
+        f = O.FORMATS[fmt]
+        units = max(1, int(sample_mb * (1 << 20) * nb / total // f.unit_bytes))
+        n_values = units * f.unit_values
+        sample.append((fmt, gen_tensor_bytes(fmt, n_values, seed * 7919 + rank * 31 + len(sample)).tobytes(),
+                       n_values))
+    nbytes = sum(len(r) for _, r, _ in sample)
+    times = []
+    for _ in range(n_steps):
+        barrier.wait()
+        t0 = time.time()
+        for fmt, raw, n_values in sample:
+            O.unpack_tensor(fmt, raw, (n_values // 256 if n_values % 256 == 0 else n_values // 32,
+                                       256 if n_values % 256 == 0 else 32), log=False)
+        times.append((t0, time.time()))
+    queue.put((nbytes, times))
+
+
+def cpu_steps(model, seed, cores, sample_mb, n_steps):
+    """Per-step (GGUF bytes, wall seconds) of `cores` workers converting their samples in
+    lock step: a step's wall time is the last end minus the first start."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    barrier = ctx.Barrier(cores)
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_cpu_step_worker, args=(model, seed, r, sample_mb, n_steps, barrier, queue))
+             for r in range(cores)]
+    for p in procs:
+        p.start()
+    res = [queue.get() for _ in procs]
+    for p in procs:
+        p.join()
+    total = sum(r[0] for r in res)
+    out = []
+    for i in range(n_steps):
+        t0 = min(r[1][i][0] for r in res)
+        t1 = max(r[1][i][1] for r in res)
+        out.append((total, t1 - t0))
+    return out
+
+
 def cpu_throughput(model, seed, cores, sample_mb=8.0, seconds=8.0, passes=0):
     """GB/s of GGUF bytes converted by `cores` spawned processes running the oracle."""
     import multiprocessing as mp
@@ -434,13 +486,11 @@ def main():
         if rank != 0:
             return 0
         cores = host_cores()
-        vals = []
-        for i in range(args.warmup + args.steps):
-            gbs, total, wall = cpu_throughput(args.model, args.seed, cores, sample_mb=4.0, passes=1)
-            if i >= args.warmup:
-                vals.append((gbs, total, wall))
-        value = statistics.median(v[0] for v in vals)
-        sample = f"per step: {cores} spawned workers x 4 MB slice of the {args.model} format mix, one pass each"
+        steps = cpu_steps(args.model, args.seed, cores, 4.0, args.warmup + args.steps)[args.warmup:]
+        vals = [(total / wall / 1e9, total, wall) for total, wall in steps]
+        value = sum(v[1] for v in vals) / sum(v[2] for v in vals) / 1e9
+        sample = (f"per step: {cores} spawned workers, each converting a 4 MB slice of the {args.model} "
+                  f"format mix (numpy oracle), steps synchronized by a barrier")
         line = {"metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(statistics.median(v[2] for v in vals) * 1e3, 2),
