@@ -31,6 +31,10 @@ __device__ __forceinline__ int f32_to_i16_x86(float x) {
 
 // ---- per-block requantization parameters (requantize_symmetric) --------------------
 
+#ifndef GQ_RQ_BRANCHLESS
+#define GQ_RQ_BRANCHLESS 1
+#endif
+
 // f32(f16(1e-4)): SCALE_EPSILON of ggml_quant.py:836 widened exactly (f16 bits 0x068E).
 constexpr float kScaleEpsilon = 1.0001659393310547e-4f;
 
@@ -69,6 +73,17 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     // since rounding is monotone the rounded quotient of the smaller one is the minimum.
     const bool need_lo = lo < static_cast<float>(lo_out) / 16.0f;
     const bool need_hi = hi > static_cast<float>(hi_out) / 16.0f;
+#if GQ_RQ_BRANCHLESS
+    // the candidate quotient is computed unconditionally and selected, which keeps the
+    // dependent chain free of divergent branches (the quotient is discarded when neither
+    // bound applies; its operands are then finite or the result is unused)
+    const float e = __fmaf_rn(-static_cast<float>(hi_out), lo, __fmul_rn(static_cast<float>(lo_out), hi));
+    const bool use_lo = need_lo && (!need_hi || e > 0.0f);
+    const float t = __fdiv_rn(static_cast<float>(use_lo ? lo_out : hi_out), use_lo ? lo : hi);
+    float sf = (need_lo || need_hi) ? fminf(16.0f, t) : 16.0f;
+    const bool big = sf > 0.98f;
+    sf = big ? fmaxf(floorf(sf), 1.0f) : sf;
+#else
     float sf = 16.0f;
     if (need_lo || need_hi) {
         const float e = __fmaf_rn(-static_cast<float>(hi_out), lo, __fmul_rn(static_cast<float>(lo_out), hi));
@@ -77,6 +92,7 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     }
     const bool big = sf > 0.98f;
     if (big) sf = fmaxf(floorf(sf), 1.0f);
+#endif
     const float rmv = __fmul_rn(r, sf);
     const int rm = __float2int_rn(rmv);
     p.sf = sf;
@@ -84,6 +100,11 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     p.round_err = fabsf(__fsub_rn(rintf(rmv), rmv));
     p.fast = big || (sf == 0.0f);
     int vmin, vmax;
+#if GQ_RQ_BRANCHLESS
+    p.sfi = p.fast ? static_cast<int>(sf) : 0;
+    vmin = (p.fast ? qmin * p.sfi : __float2int_rn(__fmul_rn(qminf, sf))) + rm;
+    vmax = (p.fast ? qmax * p.sfi : __float2int_rn(__fmul_rn(qmaxf, sf))) + rm;
+#else
     if (p.fast) {
         p.sfi = static_cast<int>(sf);
         vmin = qmin * p.sfi + rm;
@@ -93,6 +114,7 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
         vmin = __float2int_rn(__fmul_rn(qminf, sf)) + rm;
         vmax = __float2int_rn(__fmul_rn(qmaxf, sf)) + rm;
     }
+#endif
     // scale = S / sf (the original S, ggml_quant.py:882).  For an integer sf in 1..16 and a
     // finite S: q0 = S*(1/sf) and one fma correction, which equals IEEE division for every
     // f16-derived S (checked exhaustively, tests/numerics/div_by_small_int.c).

@@ -168,10 +168,17 @@ __device__ __forceinline__ uint32_t and_fresh(uint32_t a, uint32_t m) {
     return r;
 }
 
+// Recompute the lane layouts in the apply phase instead of keeping them live (1), or let
+// the compiler keep them (0).
+#ifndef GQ_FRESH_MASKS
+#define GQ_FRESH_MASKS 0
+#endif
+
 // The four 16-bit lane layouts of word i (see above).  FRESH: recompute (apply phase).
-template <bool Q5, bool FRESH = false>
+template <bool Q5, bool FRESH_ = false>
 __device__ __forceinline__ void group_layouts(const GroupWords<Q5>& q, int i, uint32_t& el, uint32_t& ol,
                                               uint32_t& eh, uint32_t& oh) {
+    constexpr bool FRESH = FRESH_ && GQ_FRESH_MASKS;
     const uint32_t w = q.w[i];
     if (!Q5) {
         if (FRESH) {
