@@ -311,11 +311,12 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
                 acc.add(pH[j].round_err, pH[j].clip_err);
             }
             constexpr uint32_t kBias = 0x400u;   // lane value q*sf + rm + bias stays in [0, 4096)
-            constexpr uint32_t kLo2 = (kBias - 128u) * 0x00010001u, kHi2 = (kBias + 127u) * 0x00010001u;
             const uint32_t sfiL = static_cast<uint32_t>(pL[j].sfi), sfiH = static_cast<uint32_t>(pH[j].sfi);
             const uint32_t KL = static_cast<uint32_t>(pL[j].rm + static_cast<int>(kBias)) * 0x00010001u;
             const uint32_t KH = static_cast<uint32_t>(pH[j].rm + static_cast<int>(kBias)) * 0x00010001u;
-            const bool plain = pL[j].fast && !pL[j].clip && pH[j].fast && !pH[j].clip;
+            // blocks with clipping or a non-integer scale factor (about 0.5%) are left to
+            // the cooperative pass below, so the per-word code here never diverges
+            const bool badL = !pL[j].fast || pL[j].clip, badH = !pH[j].fast || pH[j].clip;
             uint32_t lo[8], hi[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -327,33 +328,37 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
                 lo[i] = codes_word(el * sfiL + KL, mad_hi(ol, sfiL << 24, KL));
                 hi[i] = codes_word((eh * sfiH + (KH << 4)) >> 4, Q5 ? oh * sfiH + KH : mad_hi(oh, sfiH << 20, KH));
             }
-            if (!plain) {
-                // clipping or a non-integer scale factor (rare): redo the affected side
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    uint32_t el, ol, eh, oh;
-                    group_layouts<Q5, true>(q[j], i, el, ol, eh, oh);
-                    if (!pL[j].fast) {
-                        lo[i] = requant_word_general(codes_word(el, ol >> 8), pL[j]);
-                    } else if (pL[j].clip) {
-                        lo[i] = codes_word(vmin16(vmax16(el * sfiL + KL, kLo2), kHi2),
-                                           vmin16(vmax16(mad_hi(ol, sfiL << 24, KL), kLo2), kHi2));
-                    }
-                    if (!pH[j].fast) {
-                        hi[i] = requant_word_general(codes_word(eh >> 4, oh >> kOHShift), pH[j]);
-                    } else if (pH[j].clip) {
-                        const uint32_t ohv = Q5 ? oh * sfiH + KH : mad_hi(oh, sfiH << 20, KH);
-                        hi[i] = codes_word(vmin16(vmax16((eh * sfiH + (KH << 4)) >> 4, kLo2), kHi2),
-                                           vmin16(vmax16(ohv, kLo2), kHi2));
-                    }
-                }
-            }
-            if (valid[j]) {
-                uint8_t* base = D.codes + off;
+            uint8_t* base = D.codes + off;
+            if (valid[j] && !badL) {
                 stg128(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
                 stg128(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
+            }
+            if (valid[j] && !badH) {
                 stg128(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
                 stg128(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
+            }
+            // cooperative pass: for each lane holding such a block, lane k of the warp
+            // requantizes byte k of that lane's group with the per-value formula
+            // (ggml_quant.py:866-875), low nibble -> block 2g, high nibble -> block 2g+1
+            unsigned pending = __ballot_sync(kFull, valid[j] && (badL || badH));
+            while (pending) {
+                const int src = __ffs(pending) - 1;
+                pending &= pending - 1;
+                const int which = __shfl_sync(kFull, (badL ? 1 : 0) | (badH ? 2 : 0), src);
+                const float sL = __shfl_sync(kFull, pL[j].sf, src), sH = __shfl_sync(kFull, pH[j].sf, src);
+                const int rL = __shfl_sync(kFull, pL[j].rm, src), rH = __shfl_sync(kFull, pH[j].rm, src);
+                uint8_t* dst = reinterpret_cast<uint8_t*>(__shfl_sync(kFull, reinterpret_cast<uintptr_t>(base), src));
+                const int ssb = src >> 2, sg = src & 3;
+                const uint8_t* sbp = tile + ssb * UB;
+                const int byte = sbp[QS + 32 * sg + lane];
+                int qlo = byte & 15, qhi = byte >> 4;
+                if (Q5) {
+                    const int hb = sbp[16 + lane] >> (2 * sg);
+                    qlo |= (hb & 1) << 4;
+                    qhi |= (hb & 2) << 3;
+                }
+                if (which & 1) dst[lane] = static_cast<uint8_t>(requant_value(qlo, sL, rL, -128, 127));
+                if (which & 2) dst[32 + lane] = static_cast<uint8_t>(requant_value(qhi, sH, rH, -128, 127));
             }
         }
         if ((MODE & kOutF32) && valid[j]) {
