@@ -132,6 +132,53 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     return p;
 }
 
+// The common case of requant_block on its own: finite S and M, an integer scale factor
+// (sf > 0.98) and no code that clips.  Such a block is `good` and its fields equal
+// requant_block's; for any other block `good` is false, round_err is 0 and the other
+// fields are unspecified (the caller recomputes the block with requant_block).  sfi stays
+// in 1..16 for every input, so recip[sfi] is always in bounds.
+struct FastRequant {
+    int sfi;          // integer scale factor
+    int rm;           // int16(rint(r * sf))
+    float scale;      // S / sf
+    float round_err;  // |rm - r * sf| (good blocks), else 0
+    bool good;
+};
+
+__device__ __forceinline__ FastRequant requant_fast(float S, float M, int qmin, int qmax, int lo_out, int hi_out,
+                                                    const float* recip) {
+    FastRequant p;
+    const float s_eff = (S == 0.0f) ? ((fabsf(M) > kScaleEpsilon) ? M : kScaleEpsilon) : S;
+    const float r = __fdiv_rn(M, s_eff);
+    const float lo = __fadd_rn(static_cast<float>(qmin), r);
+    const float hi = __fadd_rn(static_cast<float>(qmax), r);
+    // sf = min(16, lo_out/lo, hi_out/hi) as in requant_block (the smaller quotient found
+    // with one exact fma); both operands of the division are positive multiples here
+    const bool need_lo = lo < static_cast<float>(lo_out) / 16.0f;
+    const bool need_hi = hi > static_cast<float>(hi_out) / 16.0f;
+    const float e = __fmaf_rn(-static_cast<float>(hi_out), lo, __fmul_rn(static_cast<float>(lo_out), hi));
+    const bool use_lo = need_lo && (!need_hi || e > 0.0f);
+    const float t = __fdiv_rn(static_cast<float>(use_lo ? lo_out : hi_out), use_lo ? lo : hi);
+    const float sf0 = (need_lo || need_hi) ? fminf(16.0f, t) : 16.0f;   // in (0, 16] or NaN
+    const bool big = sf0 > 0.98f;
+    const float sf = fmaxf(floorf(sf0), 1.0f);                          // 1..16 (NaN -> 1)
+    p.sfi = static_cast<int>(sf);
+    const float rmv = __fmul_rn(r, sf);
+    p.rm = __float2int_rn(rmv);
+    // for big blocks |r * sf| < 2200 (see requant_block), so these sums do not wrap
+    const int vmin = qmin * p.sfi + p.rm, vmax = qmax * p.sfi + p.rm;
+    const bool finite = fabsf(S) < __int_as_float(0x7f800000) && fabsf(M) < __int_as_float(0x7f800000);
+    p.good = finite && big && vmin >= lo_out && vmax <= hi_out;
+    p.round_err = p.good ? fabsf(__fsub_rn(rintf(rmv), rmv)) : 0.0f;
+    // S / sf for an integer sf and finite S: q0 = S*(1/sf) and one fma correction, exact
+    // for every f16-derived S (tests/numerics/div_by_small_int.c)
+    const float y = recip[p.sfi];
+    const float q0 = __fmul_rn(S, y);
+    const float res = __fmaf_rn(-sf, q0, S);
+    p.scale = (res == 0.0f) ? q0 : __fmaf_rn(res, y, q0);
+    return p;
+}
+
 // General per-value requant (non-integer scale factor).
 __device__ __forceinline__ int requant_value(int q, float sf, int rm, int lo_out, int hi_out) {
     const int c = f32_to_i16_x86(rintf(__fmul_rn(static_cast<float>(q), sf)));

@@ -37,6 +37,9 @@ namespace gq {
 #ifndef GQ_K45_STAGES
 #define GQ_K45_STAGES 3
 #endif
+#ifndef GQ_K45_WARPS
+#define GQ_K45_WARPS 8
+#endif
 #ifndef GQ_Q5K_SUB
 #define GQ_Q5K_SUB 1
 #endif
@@ -47,9 +50,11 @@ namespace gq {
 template <int TYPE>
 struct Fmt;
 
-#define GQ_FMT(TYPE, UNIT_BYTES, UNITS_PER_TILE, STAGES)                                  \
+#define GQ_FMT(TYPE, UNIT_BYTES, UNITS_PER_TILE, STAGES, WARPS)                           \
     template <>                                                                           \
     struct Fmt<TYPE> {                                                                    \
+        static constexpr int kWarps = WARPS;  /* warps per CTA */                         \
+        static constexpr int kThreads = 32 * WARPS;                                       \
         static constexpr int kUnitBytes = UNIT_BYTES;                                     \
         static constexpr int kUnitsPerTile = UNITS_PER_TILE;                              \
         static constexpr int kTileBytes = UNIT_BYTES * UNITS_PER_TILE;                    \
@@ -58,16 +63,16 @@ struct Fmt;
         static_assert(kTileBytes % 16 == 0, "tiles must be whole 16-byte chunks");        \
     };
 
-GQ_FMT(GQ_TYPE_Q4_K, 144, 8 * GQ_K45_SUB, GQ_K45_STAGES)   // GQ_K45_SUB sub-tiles of 8 super-blocks
-GQ_FMT(GQ_TYPE_Q5_K, 176, 8 * GQ_Q5K_SUB, GQ_Q5K_STAGES)
-GQ_FMT(GQ_TYPE_Q6_K, 210, 8, 3)   // 128 blocks of 16 per tile
-GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4)   // 32 blocks of 32 per tile
-GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4)
-GQ_FMT(GQ_TYPE_Q4_1, 20, 32, 4)   // 32 blocks of 32 per tile, one per lane
-GQ_FMT(GQ_TYPE_Q5_0, 22, 32, 4)
-GQ_FMT(GQ_TYPE_Q5_1, 24, 32, 4)
-GQ_FMT(GQ_TYPE_Q2_K, 84, 8, 4)    // 128 blocks of 16 per tile, one per lane and round
-GQ_FMT(GQ_TYPE_Q3_K, 110, 8, 4)
+GQ_FMT(GQ_TYPE_Q4_K, 144, 8 * GQ_K45_SUB, GQ_K45_STAGES, GQ_K45_WARPS)   // sub-tiles of 8 super-blocks
+GQ_FMT(GQ_TYPE_Q5_K, 176, 8 * GQ_Q5K_SUB, GQ_Q5K_STAGES, 8)
+GQ_FMT(GQ_TYPE_Q6_K, 210, 8, 3, 8)   // 128 blocks of 16 per tile
+GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4, 8)   // 32 blocks of 32 per tile
+GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4, 8)
+GQ_FMT(GQ_TYPE_Q4_1, 20, 32, 4, 8)   // 32 blocks of 32 per tile, one per lane
+GQ_FMT(GQ_TYPE_Q5_0, 22, 32, 4, 8)
+GQ_FMT(GQ_TYPE_Q5_1, 24, 32, 4, 8)
+GQ_FMT(GQ_TYPE_Q2_K, 84, 8, 4, 8)    // 128 blocks of 16 per tile, one per lane and round
+GQ_FMT(GQ_TYPE_Q3_K, 110, 8, 4, 8)
 #undef GQ_FMT
 
 // Minimum resident CTAs per SM the Q4_K kernel is compiled for (caps its registers; the
@@ -201,11 +206,52 @@ __device__ __forceinline__ void group_layouts(const GroupWords<Q5>& q, int i, ui
     }
 }
 
-// A lane owns G groups: group j is super-block lane/4 + 8j, group g = lane%4 of it.  The
-// min/max scans of all groups come first, then the 2G independent requantization chains
-// (long dependent sequences of divisions and roundings) are issued together so that they
-// hide each other's latency, then each group is requantized from its raw words.
-template <bool Q5, int MODE, int G>
+// Block constants of block b (0..7) of a Q4_K / Q5_K super-block, read by every lane of
+// the warp: S = f16(sc * d) and M = -f16(m * dmin) (ggml_quant.py:352-375, 771-777).
+__device__ __forceinline__ void k45_block_constants(const uint8_t* sbp, int b, float& S, float& M) {
+    const uint8_t* sc12 = sbp + 4;
+    int sc, mn;
+    if (b < 4) {
+        sc = sc12[b] & 0x3F;
+        mn = sc12[b + 4] & 0x3F;
+    } else {
+        sc = (sc12[b + 4] & 0x0F) | ((sc12[b - 4] >> 6) << 4);
+        mn = (sc12[b + 4] >> 4) | ((sc12[b] >> 6) << 4);
+    }
+    const uint32_t hdr = lds32(sbp);
+    S = round_to_f16(__fmul_rn(static_cast<float>(sc), h2f(hdr)));
+    M = -round_to_f16(__fmul_rn(static_cast<float>(mn), h2f(hdr >> 16)));
+}
+
+// Exact requantization of one block of the sub-tile by the whole warp (the blocks that
+// requant_fast leaves: non-integer scale factor, clipping, non-finite constants).  Lane k
+// takes value k: the low (H = false) or high nibble of byte k of the block's group,
+// with Q5_K's fifth bit; min / max come from warp reductions, then requant_block and the
+// per-value formula (ggml_quant.py:785-886).  Returns the block's diagnostics.
+template <bool Q5>
+__device__ __noinline__ gq_diag_t k45_block_exact(const uint8_t* sbp, int g, bool H, int lane, uint8_t* codes,
+                                                  float* scale, const float* recip) {
+    constexpr int QS = Q5 ? 48 : 16;
+    const int byte = sbp[QS + 32 * g + lane];
+    int q = H ? (byte >> 4) : (byte & 15);
+    if (Q5) q |= ((sbp[16 + lane] >> (2 * g + (H ? 1 : 0))) & 1) << 4;
+    const int qmin = static_cast<int>(__reduce_min_sync(kFull, static_cast<unsigned>(q)));
+    const int qmax = static_cast<int>(__reduce_max_sync(kFull, static_cast<unsigned>(q)));
+    float S, M;
+    k45_block_constants(sbp, 2 * g + (H ? 1 : 0), S, M);
+    const Requant p = requant_block(S, M, qmin, qmax, -128, 127, recip);
+    codes[lane] = static_cast<uint8_t>(requant_value(q, p.sf, p.rm, -128, 127));
+    if (lane == 0) *scale = p.scale;
+    gq_diag_t diag;
+    diag.round_err_bits = __float_as_uint(p.round_err);
+    diag.clip_err = p.clip_err;
+    return diag;
+}
+
+// Lane l owns group l of an 8-super-block sub-tile: super-block l/4, group g = l%4, i.e.
+// block 2g (low nibbles) and block 2g+1 (high nibbles).  The min / max scan comes first,
+// then the two requantization chains, then the codes from the raw words.
+template <bool Q5, int MODE>
 __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int nunits,
                                             const uint8_t* tile, int lane, DiagAcc& acc,
                                             const float* recip) {
@@ -215,175 +261,145 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
     const int g = lane & 3;
     const uint32_t sel = (g & 1) ? 0x4432u : 0x4410u;
 
-    GroupWords<Q5> q[G];
-    int scL[G], scH[G], mnL[G], mnH[G];
-    float d[G], dmin[G];
-    bool valid[G];
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-        const int sb = (lane >> 2) + 8 * j;
-        valid[j] = sb < nunits;
-        const uint8_t* sbp = tile + sb * UB;
-        // 6-bit scale / min of blocks 2g and 2g+1 (ggml_quant.py:352-375): byte j' of the
-        // first / second / third word of the 12 scale bytes, j' = (2g)&3 and (2g)&3 + 1
-        const uint32_t hdr = lds32(sbp);
-        const uint32_t b0 = __byte_perm(lds32(sbp + 4), 0, sel);
-        const uint32_t b1 = __byte_perm(lds32(sbp + 8), 0, sel);
-        const uint32_t b2 = __byte_perm(lds32(sbp + 12), 0, sel);
-        const uint32_t sc2 = (g < 2) ? (b0 & 0x3F3Fu) : ((b2 & 0x0F0Fu) | ((b0 >> 2) & 0x3030u));
-        const uint32_t mn2 = (g < 2) ? (b1 & 0x3F3Fu) : (((b2 >> 4) & 0x0F0Fu) | ((b1 >> 2) & 0x3030u));
-        d[j] = h2f(hdr);
-        dmin[j] = h2f(hdr >> 16);
-        scL[j] = sc2 & 0xFF;
-        scH[j] = sc2 >> 8;
-        mnL[j] = mn2 & 0xFF;
-        mnH[j] = mn2 >> 8;
+    const int sb = lane >> 2;
+    const bool valid = sb < nunits;
+    const uint8_t* sbp = tile + sb * UB;
+    // 6-bit scale / min of blocks 2g and 2g+1 (ggml_quant.py:352-375): byte j' of the
+    // first / second / third word of the 12 scale bytes, j' = (2g)&3 and (2g)&3 + 1
+    const uint32_t hdr = lds32(sbp);
+    const uint32_t b0 = __byte_perm(lds32(sbp + 4), 0, sel);
+    const uint32_t b1 = __byte_perm(lds32(sbp + 8), 0, sel);
+    const uint32_t b2 = __byte_perm(lds32(sbp + 12), 0, sel);
+    const uint32_t sc2 = (g < 2) ? (b0 & 0x3F3Fu) : ((b2 & 0x0F0Fu) | ((b0 >> 2) & 0x3030u));
+    const uint32_t mn2 = (g < 2) ? (b1 & 0x3F3Fu) : (((b2 >> 4) & 0x0F0Fu) | ((b1 >> 2) & 0x3030u));
+    const float d = h2f(hdr);
+    const float dmin = h2f(hdr >> 16);
+    const int scL = sc2 & 0xFF, scH = sc2 >> 8, mnL = mn2 & 0xFF, mnH = mn2 >> 8;
+    GroupWords<Q5> q;
+    {
         const uint8_t* qp = sbp + QS + 32 * g;
         const uint4 qa = lds128(qp), qb = lds128(qp + 16);
-        q[j].w[0] = qa.x; q[j].w[1] = qa.y; q[j].w[2] = qa.z; q[j].w[3] = qa.w;
-        q[j].w[4] = qb.x; q[j].w[5] = qb.y; q[j].w[6] = qb.z; q[j].w[7] = qb.w;
+        q.w[0] = qa.x; q.w[1] = qa.y; q.w[2] = qa.z; q.w[3] = qa.w;
+        q.w[4] = qb.x; q.w[5] = qb.y; q.w[6] = qb.z; q.w[7] = qb.w;
         if (Q5) {
             // fifth bit of block k is bit k of qh[j] (ggml_quant.py:311-349): bit 2g for the
             // low nibbles, 2g+1 for the high nibbles
             const uint4 ha = lds128(sbp + 16), hb = lds128(sbp + 32);
             const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) q[j].h[Q5 ? i : 0] = hw[i] >> (2 * g);
+            for (int i = 0; i < 8; ++i) q.h[Q5 ? i : 0] = hw[i] >> (2 * g);
         }
     }
 
-    Requant pL[G], pH[G];
+    const int64_t ou = permute_unit(D, unit0 + sb);
+    const int64_t off = ou * 256 + 64 * g;   // codes / values of block 2g, then 2g+1
     if (MODE & kOutCodes) {
-        int qminL[G], qmaxL[G], qminH[G], qmaxH[G];
-#pragma unroll
-        for (int j = 0; j < G; ++j) {
-            // block min / max of the codes (16-bit-lane SIMD), two words per step
-            uint32_t mnEL, mxEL, mnOL, mxOL, mnEH, mxEH, mnOH, mxOH;
-            {
-                uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
-                group_layouts(q[j], 0, a0, a1, a2, a3);
-                group_layouts(q[j], 1, c0, c1, c2, c3);
-                mnEL = vmin16(a0, c0); mxEL = vmax16(a0, c0);
-                mnOL = vmin16(a1, c1); mxOL = vmax16(a1, c1);
-                mnEH = vmin16(a2, c2); mxEH = vmax16(a2, c2);
-                mnOH = vmin16(a3, c3); mxOH = vmax16(a3, c3);
-            }
-#pragma unroll
-            for (int i = 2; i < 8; i += 2) {
-                uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
-                group_layouts(q[j], i, a0, a1, a2, a3);
-                group_layouts(q[j], i + 1, c0, c1, c2, c3);
-                mnEL = vmin16(mnEL, a0, c0); mxEL = vmax16(mxEL, a0, c0);
-                mnOL = vmin16(mnOL, a1, c1); mxOL = vmax16(mxOL, a1, c1);
-                mnEH = vmin16(mnEH, a2, c2); mxEH = vmax16(mxEH, a2, c2);
-                mnOH = vmin16(mnOH, a3, c3); mxOH = vmax16(mxOH, a3, c3);
-            }
-            const uint32_t aminL = vmin16(mnEL, mnOL >> 8), amaxL = vmax16(mxEL, mxOL >> 8);
-            const uint32_t aminH = vmin16(mnEH >> 4, mnOH >> kOHShift);
-            const uint32_t amaxH = vmax16(mxEH >> 4, mxOH >> kOHShift);
-            qminL[j] = min(aminL & 0xFFFF, aminL >> 16);
-            qmaxL[j] = max(amaxL & 0xFFFF, amaxL >> 16);
-            qminH[j] = min(aminH & 0xFFFF, aminH >> 16);
-            qmaxH[j] = max(amaxH & 0xFFFF, amaxH >> 16);
+        // block min / max of the codes (16-bit-lane SIMD), two words per step
+        uint32_t mnEL, mxEL, mnOL, mxOL, mnEH, mxEH, mnOH, mxOH;
+        {
+            uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
+            group_layouts(q, 0, a0, a1, a2, a3);
+            group_layouts(q, 1, c0, c1, c2, c3);
+            mnEL = vmin16(a0, c0); mxEL = vmax16(a0, c0);
+            mnOL = vmin16(a1, c1); mxOL = vmax16(a1, c1);
+            mnEH = vmin16(a2, c2); mxEH = vmax16(a2, c2);
+            mnOH = vmin16(a3, c3); mxOH = vmax16(a3, c3);
         }
 #pragma unroll
-        for (int j = 0; j < G; ++j) {
-            // block constants f16(f32 product), min negated (ggml_quant.py:771-777), then
-            // requantize_symmetric (ggml_quant.py:785-886)
-            const float SL = round_to_f16(__fmul_rn(static_cast<float>(scL[j]), d[j]));
-            const float SH = round_to_f16(__fmul_rn(static_cast<float>(scH[j]), d[j]));
-            const float ML = -round_to_f16(__fmul_rn(static_cast<float>(mnL[j]), dmin[j]));
-            const float MH = -round_to_f16(__fmul_rn(static_cast<float>(mnH[j]), dmin[j]));
-            pL[j] = requant_block(SL, ML, qminL[j], qmaxL[j], -128, 127, recip);
-            pH[j] = requant_block(SH, MH, qminH[j], qmaxH[j], -128, 127, recip);
+        for (int i = 2; i < 8; i += 2) {
+            uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
+            group_layouts(q, i, a0, a1, a2, a3);
+            group_layouts(q, i + 1, c0, c1, c2, c3);
+            mnEL = vmin16(mnEL, a0, c0); mxEL = vmax16(mxEL, a0, c0);
+            mnOL = vmin16(mnOL, a1, c1); mxOL = vmax16(mxOL, a1, c1);
+            mnEH = vmin16(mnEH, a2, c2); mxEH = vmax16(mxEH, a2, c2);
+            mnOH = vmin16(mnOH, a3, c3); mxOH = vmax16(mxOH, a3, c3);
+        }
+        const uint32_t aminL = vmin16(mnEL, mnOL >> 8), amaxL = vmax16(mxEL, mxOL >> 8);
+        const uint32_t aminH = vmin16(mnEH >> 4, mnOH >> kOHShift);
+        const uint32_t amaxH = vmax16(mxEH >> 4, mxOH >> kOHShift);
+        const int qminL = min(aminL & 0xFFFF, aminL >> 16), qmaxL = max(amaxL & 0xFFFF, amaxL >> 16);
+        const int qminH = min(aminH & 0xFFFF, aminH >> 16), qmaxH = max(amaxH & 0xFFFF, amaxH >> 16);
+
+        // block constants f16(f32 product), min negated (ggml_quant.py:771-777), then
+        // requantize_symmetric (ggml_quant.py:785-886) for the common case
+        const float SL = round_to_f16(__fmul_rn(static_cast<float>(scL), d));
+        const float SH = round_to_f16(__fmul_rn(static_cast<float>(scH), d));
+        const float ML = -round_to_f16(__fmul_rn(static_cast<float>(mnL), dmin));
+        const float MH = -round_to_f16(__fmul_rn(static_cast<float>(mnH), dmin));
+        const FastRequant pL = requant_fast(SL, ML, qminL, qmaxL, -128, 127, recip);
+        const FastRequant pH = requant_fast(SH, MH, qminH, qmaxH, -128, 127, recip);
+        if (valid) {
+            *reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g) = make_float2(pL.scale, pH.scale);
+            acc.add(fmaxf(pL.round_err, pH.round_err), 0);
+        }
+        constexpr uint32_t kBias = 0x400u;   // lane value q*sf + rm + bias stays in [0, 4096)
+        const uint32_t sfiL = static_cast<uint32_t>(pL.sfi), sfiH = static_cast<uint32_t>(pH.sfi);
+        const uint32_t KL = static_cast<uint32_t>(pL.rm + static_cast<int>(kBias)) * 0x00010001u;
+        const uint32_t KH = static_cast<uint32_t>(pH.rm + static_cast<int>(kBias)) * 0x00010001u;
+        uint32_t lo[8], hi[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            // low nibbles: EL*sf + K and high32(OL * (sf << 24)) + K; high nibbles:
+            // (EH*sf + 16K) >> 4 and high32(OH * (sf << 20)) + K (Q5_K: OH*sf + K); the
+            // low bytes of the 16-bit lanes are the codes (the bias has a zero low byte)
+            uint32_t el, ol, eh, oh;
+            group_layouts<Q5, true>(q, i, el, ol, eh, oh);
+            lo[i] = codes_word(el * sfiL + KL, mad_hi(ol, sfiL << 24, KL));
+            hi[i] = codes_word((eh * sfiH + (KH << 4)) >> 4, Q5 ? oh * sfiH + KH : mad_hi(oh, sfiH << 20, KH));
+        }
+        uint8_t* base = D.codes + off;
+        if (valid && pL.good) {
+            stg128(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
+            stg128(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
+        }
+        if (valid && pH.good) {
+            stg128(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
+            stg128(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
+        }
+        // the other blocks (about 0.5%): one warp pass each, after the scale stores above
+        unsigned pending = __ballot_sync(kFull, valid && !(pL.good && pH.good));
+        if (pending) __syncwarp();
+        while (pending) {
+            const int src = __ffs(pending) - 1;
+            pending &= pending - 1;
+            const int which = __shfl_sync(kFull, (pL.good ? 0 : 1) | (pH.good ? 0 : 2), src);
+            const int64_t soff = __shfl_sync(kFull, off, src);
+            const uint8_t* ssbp = tile + (src >> 2) * UB;
+            if (which & 1) {
+                const gq_diag_t e = k45_block_exact<Q5>(ssbp, src & 3, false, lane, D.codes + soff,
+                                                        D.scales + (soff >> 5), recip);
+                acc.add(__uint_as_float(e.round_err_bits), e.clip_err);
+            }
+            if (which & 2) {
+                const gq_diag_t e = k45_block_exact<Q5>(ssbp, src & 3, true, lane, D.codes + soff + 32,
+                                                        D.scales + (soff >> 5) + 1, recip);
+                acc.add(__uint_as_float(e.round_err_bits), e.clip_err);
+            }
         }
     }
-
+    if ((MODE & kOutF32) && valid) {
+        // gguf-py dequantize: (d*sc)*q - dmin*m, each product rounded
+        // (Q4_K/Q5_K.dequantize_blocks)
+        const float dsL = __fmul_rn(d, static_cast<float>(scL));
+        const float dmL = __fmul_rn(dmin, static_cast<float>(mnL));
+        const float dsH = __fmul_rn(d, static_cast<float>(scH));
+        const float dmH = __fmul_rn(dmin, static_cast<float>(mnH));
+        float* vdst = D.values + off;
 #pragma unroll
-    for (int j = 0; j < G; ++j) {
-        const int sb = (lane >> 2) + 8 * j;
-        const int64_t ou = permute_unit(D, unit0 + sb);
-        const int64_t off = ou * 256 + 64 * g;   // codes / values of block 2g, then 2g+1
-        if (MODE & kOutCodes) {
-            if (valid[j]) {
-                *reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g) = make_float2(pL[j].scale, pH[j].scale);
-                acc.add(pL[j].round_err, pL[j].clip_err);
-                acc.add(pH[j].round_err, pH[j].clip_err);
-            }
-            constexpr uint32_t kBias = 0x400u;   // lane value q*sf + rm + bias stays in [0, 4096)
-            const uint32_t sfiL = static_cast<uint32_t>(pL[j].sfi), sfiH = static_cast<uint32_t>(pH[j].sfi);
-            const uint32_t KL = static_cast<uint32_t>(pL[j].rm + static_cast<int>(kBias)) * 0x00010001u;
-            const uint32_t KH = static_cast<uint32_t>(pH[j].rm + static_cast<int>(kBias)) * 0x00010001u;
-            // blocks with clipping or a non-integer scale factor (about 0.5%) are left to
-            // the cooperative pass below, so the per-word code here never diverges
-            const bool badL = !pL[j].fast || pL[j].clip, badH = !pH[j].fast || pH[j].clip;
-            uint32_t lo[8], hi[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                // low nibbles: EL*sf + K and high32(OL * (sf << 24)) + K; high nibbles:
-                // (EH*sf + 16K) >> 4 and high32(OH * (sf << 20)) + K (Q5_K: OH*sf + K); the
-                // low bytes of the 16-bit lanes are the codes (the bias has a zero low byte)
-                uint32_t el, ol, eh, oh;
-                group_layouts<Q5, true>(q[j], i, el, ol, eh, oh);
-                lo[i] = codes_word(el * sfiL + KL, mad_hi(ol, sfiL << 24, KL));
-                hi[i] = codes_word((eh * sfiH + (KH << 4)) >> 4, Q5 ? oh * sfiH + KH : mad_hi(oh, sfiH << 20, KH));
-            }
-            uint8_t* base = D.codes + off;
-            if (valid[j] && !badL) {
-                stg128(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
-                stg128(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
-            }
-            if (valid[j] && !badH) {
-                stg128(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
-                stg128(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
-            }
-            // cooperative pass: for each lane holding such a block, lane k of the warp
-            // requantizes byte k of that lane's group with the per-value formula
-            // (ggml_quant.py:866-875), low nibble -> block 2g, high nibble -> block 2g+1
-            unsigned pending = __ballot_sync(kFull, valid[j] && (badL || badH));
-            while (pending) {
-                const int src = __ffs(pending) - 1;
-                pending &= pending - 1;
-                const int which = __shfl_sync(kFull, (badL ? 1 : 0) | (badH ? 2 : 0), src);
-                const float sL = __shfl_sync(kFull, pL[j].sf, src), sH = __shfl_sync(kFull, pH[j].sf, src);
-                const int rL = __shfl_sync(kFull, pL[j].rm, src), rH = __shfl_sync(kFull, pH[j].rm, src);
-                uint8_t* dst = reinterpret_cast<uint8_t*>(__shfl_sync(kFull, reinterpret_cast<uintptr_t>(base), src));
-                const int ssb = src >> 2, sg = src & 3;
-                const uint8_t* sbp = tile + ssb * UB;
-                const int byte = sbp[QS + 32 * sg + lane];
-                int qlo = byte & 15, qhi = byte >> 4;
-                if (Q5) {
-                    const int hb = sbp[16 + lane] >> (2 * sg);
-                    qlo |= (hb & 1) << 4;
-                    qhi |= (hb & 2) << 3;
-                }
-                if (which & 1) dst[lane] = static_cast<uint8_t>(requant_value(qlo, sL, rL, -128, 127));
-                if (which & 2) dst[32 + lane] = static_cast<uint8_t>(requant_value(qhi, sH, rH, -128, 127));
-            }
-        }
-        if ((MODE & kOutF32) && valid[j]) {
-            // gguf-py dequantize: (d*sc)*q - dmin*m, each product rounded
-            // (Q4_K/Q5_K.dequantize_blocks)
-            const float dsL = __fmul_rn(d[j], static_cast<float>(scL[j]));
-            const float dmL = __fmul_rn(dmin[j], static_cast<float>(mnL[j]));
-            const float dsH = __fmul_rn(d[j], static_cast<float>(scH[j]));
-            const float dmH = __fmul_rn(dmin[j], static_cast<float>(mnH[j]));
-            float* vdst = D.values + off;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                uint32_t el, ol, eh, oh;
-                group_layouts<Q5, true>(q[j], i, el, ol, eh, oh);
-                const uint32_t ql = codes_word(el, ol >> 8);
-                const uint32_t qh = codes_word(eh >> 4, oh >> kOHShift);
-                stg128f(vdst + 4 * i, __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 0))), dmL),
-                        __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 1))), dmL),
-                        __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 2))), dmL),
-                        __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 3))), dmL));
-                stg128f(vdst + 32 + 4 * i, __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 0))), dmH),
-                        __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 1))), dmH),
-                        __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 2))), dmH),
-                        __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 3))), dmH));
-            }
+        for (int i = 0; i < 8; ++i) {
+            uint32_t el, ol, eh, oh;
+            group_layouts<Q5, true>(q, i, el, ol, eh, oh);
+            const uint32_t ql = codes_word(el, ol >> 8);
+            const uint32_t qh = codes_word(eh >> 4, oh >> kOHShift);
+            stg128f(vdst + 4 * i, __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 0))), dmL),
+                    __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 1))), dmL),
+                    __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 2))), dmL),
+                    __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 3))), dmL));
+            stg128f(vdst + 32 + 4 * i, __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 0))), dmH),
+                    __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 1))), dmH),
+                    __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 2))), dmH),
+                    __fsub_rn(__fmul_rn(dsH, static_cast<float>(byte_of(qh, 3))), dmH));
         }
     }
 }
@@ -678,7 +694,9 @@ __device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int 
 // ---------------------------------------------------------------------------------------
 
 template <int TYPE, int MODE>
-__global__ void __launch_bounds__(kThreads, TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS : (TYPE == GQ_TYPE_Q5_K ? 2 : 1)) gq_convert_kernel(const __grid_constant__ GqBatch batch) {
+__global__ void __launch_bounds__(Fmt<TYPE>::kThreads,
+                                  TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS : (TYPE == GQ_TYPE_Q5_K ? 2 : 1))
+    gq_convert_kernel(const __grid_constant__ GqBatch batch) {
     using F = Fmt<TYPE>;
     extern __shared__ __align__(16) uint8_t smem[];
     // exact reciprocals 1/k, k = 1..16, for the block-scale division of requant_block
@@ -688,8 +706,8 @@ __global__ void __launch_bounds__(kThreads, TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     uint8_t* ring = smem + warp * (F::kStages * F::kStageBytes);
-    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
-    const int64_t first = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * F::kWarps;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * F::kWarps + warp;
     const int64_t total = batch.total_tiles;
 
     DescCursor issue_cur, proc_cur;
@@ -723,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS
             for (int j = 0; j < F::kUnitsPerTile / 8; ++j) {
                 const int rest = nunits - 8 * j;
                 if (rest <= 0) break;
-                process_k45<TYPE == GQ_TYPE_Q5_K, MODE, 1>(D, unit0 + 8 * j, rest < 8 ? rest : 8,
+                process_k45<TYPE == GQ_TYPE_Q5_K, MODE>(D, unit0 + 8 * j, rest < 8 ? rest : 8,
                                                            tile + 8 * j * F::kUnitBytes, lane, acc, recip);
             }
         } else if (TYPE == GQ_TYPE_Q6_K) {
@@ -845,7 +863,7 @@ DeviceInfo& device_info() {
 template <int TYPE, int MODE>
 int launch_fmt(const GqBatch& b, cudaStream_t s) {
     using F = Fmt<TYPE>;
-    constexpr int smem = kWarps * F::kStages * F::kStageBytes;
+    constexpr int smem = F::kWarps * F::kStages * F::kStageBytes;
     static_assert(smem <= 200 * 1024, "dynamic shared memory per CTA");
     static int per_sm[64] = {0};
     int dev = 0;
@@ -854,15 +872,15 @@ int launch_fmt(const GqBatch& b, cudaStream_t s) {
     if (occ == 0) {
         if (smem > 48 * 1024)
             cudaFuncSetAttribute(gq_convert_kernel<TYPE, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gq_convert_kernel<TYPE, MODE>, kThreads, smem) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gq_convert_kernel<TYPE, MODE>, F::kThreads, smem) !=
                 cudaSuccess || occ < 1)
             occ = 1;
     }
-    const int64_t want = (b.total_tiles + kWarps - 1) / kWarps;
+    const int64_t want = (b.total_tiles + F::kWarps - 1) / F::kWarps;
     const int64_t cap = static_cast<int64_t>(device_info().sms) * occ;
     const int blocks = static_cast<int>(want < cap ? want : cap);
     if (blocks <= 0) return 0;
-    gq_convert_kernel<TYPE, MODE><<<blocks, kThreads, smem, s>>>(b);
+    gq_convert_kernel<TYPE, MODE><<<blocks, F::kThreads, smem, s>>>(b);
     return static_cast<int>(cudaGetLastError());
 }
 
