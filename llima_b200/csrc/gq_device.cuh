@@ -132,6 +132,20 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     return p;
 }
 
+// RN(a / b) for f32 values a, b that are widened finite f16 values (b != 0), without a
+// branch.  y = rcp.approx(b) is within 1 ulp of 1/b; e = 1 - b*y is exact in one fma (b
+// has at most 11 significant bits); y + e*y approximates 1/b to about 2^-45 relative, and
+// a*(y + e*y) rounded once is RN(a/b), since a quotient of two 11-bit significands lies at
+// least 2^-36 (relative) from every f32 rounding midpoint.  Checked exhaustively, with any
+// y within 2 ulp, by tests/numerics/f16_quotient.c.  A zero quotient may come out with
+// either sign (no caller distinguishes them).
+__device__ __forceinline__ float quotient_f16(float a, float b) {
+    float y;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(b));
+    const float e = __fmaf_rn(-b, y, 1.0f);
+    return __fmaf_rn(a, y, __fmul_rn(a, __fmul_rn(e, y)));
+}
+
 // The common case of requant_block on its own: finite S and M, an integer scale factor
 // (sf > 0.98) and no code that clips.  Such a block is `good` and its fields equal
 // requant_block's; for any other block `good` is false, round_err is 0 and the other
@@ -149,7 +163,7 @@ __device__ __forceinline__ FastRequant requant_fast(float S, float M, int qmin, 
                                                     const float* recip) {
     FastRequant p;
     const float s_eff = (S == 0.0f) ? ((fabsf(M) > kScaleEpsilon) ? M : kScaleEpsilon) : S;
-    const float r = __fdiv_rn(M, s_eff);
+    const float r = quotient_f16(M, s_eff);
     const float lo = __fadd_rn(static_cast<float>(qmin), r);
     const float hi = __fadd_rn(static_cast<float>(qmax), r);
     // sf = min(16, lo_out/lo, hi_out/hi) as in requant_block (the smaller quotient found

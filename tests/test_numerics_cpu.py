@@ -18,3 +18,19 @@ def test_block_scale_division_by_small_integers_is_exact(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0, out.stdout
     assert "mismatches 0" in out.stdout
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_f16_quotient_is_exact(tmp_path):
+    # gq_device.cuh divides the f16-valued block constants (r = M / S) with a reciprocal
+    # approximation, its exact residual and one fma; this checks every finite f16 pair for
+    # every reciprocal within 2 ulp.
+    exe = tmp_path / "f16_quotient"
+    cmd = ["gcc", "-O2", "-ffp-contract=off", "-o", str(exe), str(HERE / "numerics" / "f16_quotient.c"), "-lm"]
+    if subprocess.run(["gcc", "-fopenmp", "-x", "c", "-", "-o", str(tmp_path / "omp")], input="int main(){return 0;}",
+                      capture_output=True, text=True).returncode == 0:
+        cmd.insert(1, "-fopenmp")
+    subprocess.run(cmd, check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout
+    assert "mismatches 0" in out.stdout
