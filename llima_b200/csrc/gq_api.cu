@@ -102,6 +102,11 @@ gq::GqDesc make_desc(const gq_tensor_t& t, const TypeInfo& ti, int64_t n_units) 
     d.units_per_row = t.cols / ti.unit_values;
     d.perm_heads = t.perm_heads;
     d.rows_per_head = t.perm_heads > 0 ? static_cast<int32_t>(t.rows / t.perm_heads) : 0;
+    // unit indices of the tensor (plus a tile of slack) fit in 31 bits: 32-bit divisions
+    if (t.perm_heads > 0 && n_units + 4096 < (int64_t(1) << 31)) {
+        gq::fast_div_params(static_cast<uint32_t>(d.units_per_row), d.upr_mul, d.upr_shift);
+        gq::fast_div_params(static_cast<uint32_t>(d.rows_per_head), d.rph_mul, d.rph_shift);
+    }
     return d;
 }
 

@@ -316,8 +316,23 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8
 
 // Output unit index after the llama q/k head permutation (gguf_conversion.py:314-332):
 // row h*D + 2a + t moves to h*D + t*D/2 + a.
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, uint32_t mul, uint32_t shift) {
+    const uint32_t t1 = __umulhi(mul, n);
+    return (t1 + ((n - t1) >> (shift & 0xFF))) >> (shift >> 8);
+}
+
 __device__ __forceinline__ int64_t permute_unit(const GqDesc& d, int64_t unit) {
     if (d.perm_heads == 0) return unit;
+    if (d.upr_mul != 0) {
+        const uint32_t upr = static_cast<uint32_t>(d.units_per_row), rph = static_cast<uint32_t>(d.rows_per_head);
+        const uint32_t u = static_cast<uint32_t>(unit);
+        const uint32_t row = fast_div(u, d.upr_mul, d.upr_shift);
+        const uint32_t col = u - row * upr;
+        const uint32_t head = fast_div(row, d.rph_mul, d.rph_shift);
+        const uint32_t i = row - head * rph;
+        const uint32_t out_row = head * rph + (i & 1) * (rph >> 1) + (i >> 1);
+        return static_cast<int64_t>(out_row * upr + col);
+    }
     const int64_t row = unit / d.units_per_row;
     const int64_t col = unit - row * d.units_per_row;
     const int64_t head = row / d.rows_per_head;

@@ -21,7 +21,21 @@ struct GqDesc {
     int64_t units_per_row;   // for the head permutation
     int32_t perm_heads;      // 0: no permutation
     int32_t rows_per_head;   // head_dim of the permuted rows
+    // 32-bit division by units_per_row and rows_per_head as multiply-high and shifts
+    // (Granlund and Montgomery, "Division by invariant integers using multiplication",
+    // 1994, figure 4.1); upr_mul == 0 when the unit indices do not fit (64-bit path)
+    uint32_t upr_mul, upr_shift;   // shift: sh1 | sh2 << 8
+    uint32_t rph_mul, rph_shift;
 };
+
+// Multiplier and shifts of the invariant-divisor method for 32-bit n and divisor d >= 1:
+// l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1, sh1 = min(l, 1), sh2 = max(l - 1, 0).
+inline void fast_div_params(uint32_t d, uint32_t& mul, uint32_t& shift) {
+    int l = 0;
+    while (l < 32 && (uint64_t(1) << l) < d) ++l;
+    mul = static_cast<uint32_t>(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
+    shift = static_cast<uint32_t>(l < 1 ? l : 1) | (static_cast<uint32_t>(l > 1 ? l - 1 : 0) << 8);
+}
 
 // Kernel parameter block (passed by value; larger than 4 KB needs CUDA >= 12.1).
 constexpr int kMaxDesc = 256;

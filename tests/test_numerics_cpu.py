@@ -34,3 +34,15 @@ def test_f16_quotient_is_exact(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0, out.stdout
     assert "mismatches 0" in out.stdout
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_invariant_divisor_parameters(tmp_path):
+    # the q/k head permutation divides unit and row indices by multiply-high and shifts
+    exe = tmp_path / "fast_div"
+    root = HERE.parent
+    subprocess.run(["g++", "-O2", "-std=c++17", "-I", str(root / "llima_b200" / "csrc"), "-o", str(exe),
+                    str(HERE / "numerics" / "fast_div.cpp")], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout
+    assert "mismatches 0" in out.stdout
