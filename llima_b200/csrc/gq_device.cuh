@@ -156,7 +156,10 @@ struct FastRequant {
     int rm;           // int16(rint(r * sf))
     float scale;      // S / sf
     float round_err;  // |rm - r * sf| (good blocks), else 0
+    float r;          // M / S' (exact when `finite`)
+    float sf0;        // min(16, lo_out/lo, hi_out/hi) before the integer rounding (exact when `finite`)
     bool good;
+    bool finite;      // S and M are finite
 };
 
 __device__ __forceinline__ FastRequant requant_fast(float S, float M, int qmin, int qmax, int lo_out, int hi_out,
@@ -183,6 +186,9 @@ __device__ __forceinline__ FastRequant requant_fast(float S, float M, int qmin, 
     const int vmin = qmin * p.sfi + p.rm, vmax = qmax * p.sfi + p.rm;
     const bool finite = fabsf(S) < __int_as_float(0x7f800000) && fabsf(M) < __int_as_float(0x7f800000);
     p.good = finite && big && vmin >= lo_out && vmax <= hi_out;
+    p.finite = finite;
+    p.r = r;
+    p.sf0 = sf0;
     p.round_err = p.good ? fabsf(__fsub_rn(rintf(rmv), rmv)) : 0.0f;
     // S / sf for an integer sf and finite S: q0 = S*(1/sf) and one fma correction, exact
     // for every f16-derived S (tests/numerics/div_by_small_int.c)
@@ -191,6 +197,28 @@ __device__ __forceinline__ FastRequant requant_fast(float S, float M, int qmin, 
     const float res = __fmaf_rn(-sf, q0, S);
     p.scale = (res == 0.0f) ? q0 : __fmaf_rn(res, y, q0);
     return p;
+}
+
+// Finish one block whose S and M are finite but that is not `good` (non-integer scale
+// factor or clipping), one value per lane of the warp, from requant_fast's exact r and
+// sf0 (ggml_quant.py:859-882): sf, rm and the block scale as requant_block derives them,
+// the per-value codes and the clipping error as the largest |clip(v) - v| of the block.
+// Returns the block's rounding and clipping errors (the same in every lane).
+__device__ __forceinline__ gq_diag_t finish_block(int q, float S, float r, float sf0, int lo_out, int hi_out,
+                                                  uint8_t* code, float* scale, int lane) {
+    const bool big = sf0 > 0.98f;
+    const float sf = big ? fmaxf(floorf(sf0), 1.0f) : sf0;
+    const float rmv = __fmul_rn(r, sf);
+    const int rm = __float2int_rn(rmv);   // |r * sf| < 2200 for finite r (see requant_block)
+    const int c = f32_to_i16_x86(rintf(__fmul_rn(static_cast<float>(q), sf)));
+    const int u = static_cast<int>(static_cast<short>(c + rm));
+    const int v = min(max(u, lo_out), hi_out);
+    *code = static_cast<uint8_t>(v);
+    if (lane == 0) *scale = __fdiv_rn(S, sf);
+    gq_diag_t e;
+    e.round_err_bits = __float_as_uint(fabsf(__fsub_rn(rintf(rmv), rmv)));
+    e.clip_err = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(abs(v - u))));
+    return e;
 }
 
 // General per-value requant (non-integer scale factor).

@@ -357,23 +357,40 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
             stg128(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
             stg128(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
         }
-        // the other blocks (about 0.5%): one warp pass each, after the scale stores above
+        // the other blocks (about 0.5%): one warp pass each, after the scale stores above;
+        // a block with finite constants is finished from its lane's r and sf0, one with a
+        // non-finite S or M is recomputed from the tile
         unsigned pending = __ballot_sync(kFull, valid && !(pL.good && pH.good));
         if (pending) __syncwarp();
         while (pending) {
             const int src = __ffs(pending) - 1;
             pending &= pending - 1;
-            const int which = __shfl_sync(kFull, (pL.good ? 0 : 1) | (pH.good ? 0 : 2), src);
+            const int which = __shfl_sync(kFull, (pL.good ? 0 : 1) | (pH.good ? 0 : 2) | (pL.finite ? 0 : 4) |
+                                                     (pH.finite ? 0 : 8), src);
             const int64_t soff = __shfl_sync(kFull, off, src);
+            const int sg = src & 3;
             const uint8_t* ssbp = tile + (src >> 2) * UB;
-            if (which & 1) {
-                const gq_diag_t e = k45_block_exact<Q5>(ssbp, src & 3, false, lane, D.codes + soff,
-                                                        D.scales + (soff >> 5), recip);
-                acc.add(__uint_as_float(e.round_err_bits), e.clip_err);
+            const int byte = ssbp[QS + 32 * sg + lane];
+            int qlo = byte & 15, qhi = byte >> 4;
+            if (Q5) {
+                const int hb = ssbp[16 + lane] >> (2 * sg);
+                qlo |= (hb & 1) << 4;
+                qhi |= (hb & 2) << 3;
             }
-            if (which & 2) {
-                const gq_diag_t e = k45_block_exact<Q5>(ssbp, src & 3, true, lane, D.codes + soff + 32,
-                                                        D.scales + (soff >> 5) + 1, recip);
+#pragma unroll
+            for (int side = 0; side < 2; ++side) {
+                if (!(which & (1 << side))) continue;
+                gq_diag_t e;
+                if (which & (4 << side)) {
+                    e = k45_block_exact<Q5>(ssbp, sg, side == 1, lane, D.codes + soff + 32 * side,
+                                            D.scales + (soff >> 5) + side, recip);
+                } else {
+                    const float bS = __shfl_sync(kFull, side ? SH : SL, src);
+                    const float br = __shfl_sync(kFull, side ? pH.r : pL.r, src);
+                    const float bsf0 = __shfl_sync(kFull, side ? pH.sf0 : pL.sf0, src);
+                    e = finish_block(side ? qhi : qlo, bS, br, bsf0, -128, 127, D.codes + soff + 32 * side + lane,
+                                     D.scales + (soff >> 5) + side, lane);
+                }
                 acc.add(__uint_as_float(e.round_err_bits), e.clip_err);
             }
         }
