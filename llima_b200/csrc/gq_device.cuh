@@ -29,6 +29,31 @@ __device__ __forceinline__ int f32_to_i16_x86(float x) {
     return static_cast<int>(static_cast<short>(__float2int_rz(x)));
 }
 
+// ---- global memory --------------------------------------------------------------------
+
+// Output stores name the global state space (st.global) rather than going through a
+// generic pointer, so that the compiler knows they cannot alias the shared-memory tiles.
+// Policy: 1 write-back (default), 2 cache-global, 3 streaming.
+#ifndef GQ_STORE_POLICY
+#define GQ_STORE_POLICY 1
+#endif
+template <class T>
+__device__ __forceinline__ void st_global(T* p, T v) {
+#if GQ_STORE_POLICY == 3
+    __stcs(p, v);
+#elif GQ_STORE_POLICY == 2
+    __stcg(p, v);
+#elif GQ_STORE_POLICY == 1
+    __stwb(p, v);
+#else
+    *p = v;
+#endif
+}
+__device__ __forceinline__ void stg128(void* p, uint4 v) { st_global(reinterpret_cast<uint4*>(p), v); }
+__device__ __forceinline__ void stg128f(float* p, float a, float b, float c, float d) {
+    st_global(reinterpret_cast<float4*>(p), make_float4(a, b, c, d));
+}
+
 // ---- per-block requantization parameters (requantize_symmetric) --------------------
 
 #ifndef GQ_RQ_BRANCHLESS
@@ -213,8 +238,8 @@ __device__ __forceinline__ gq_diag_t finish_block(int q, float S, float r, float
     const int c = f32_to_i16_x86(rintf(__fmul_rn(static_cast<float>(q), sf)));
     const int u = static_cast<int>(static_cast<short>(c + rm));
     const int v = min(max(u, lo_out), hi_out);
-    *code = static_cast<uint8_t>(v);
-    if (lane == 0) *scale = __fdiv_rn(S, sf);
+    st_global(code, static_cast<uint8_t>(v));
+    if (lane == 0) st_global(scale, __fdiv_rn(S, sf));
     gq_diag_t e;
     e.round_err_bits = __float_as_uint(fabsf(__fsub_rn(rintf(rmv), rmv)));
     e.clip_err = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(abs(v - u))));
@@ -317,15 +342,6 @@ __device__ __forceinline__ uint4 lds128_align2(const uint8_t* p) {
     r.z = __funnelshift_r(w2, w3, sh);
     r.w = __funnelshift_r(w3, w4, sh);
     return r;
-}
-
-// ---- global memory --------------------------------------------------------------------
-
-__device__ __forceinline__ void stg128(void* p, uint4 v) {
-    *reinterpret_cast<uint4*>(p) = v;
-}
-__device__ __forceinline__ void stg128f(float* p, float a, float b, float c, float d) {
-    *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
 }
 
 // cp.async of one 16-byte chunk, reading only `src_bytes` (1..16) bytes; the rest of the

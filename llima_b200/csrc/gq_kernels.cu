@@ -40,6 +40,12 @@ namespace gq {
 #ifndef GQ_K45_WARPS
 #define GQ_K45_WARPS 8
 #endif
+#ifndef GQ_Q6K_SUB
+#define GQ_Q6K_SUB 1
+#endif
+#ifndef GQ_Q6K_STAGES
+#define GQ_Q6K_STAGES 3
+#endif
 #ifndef GQ_Q5K_SUB
 #define GQ_Q5K_SUB 1
 #endif
@@ -65,7 +71,7 @@ struct Fmt;
 
 GQ_FMT(GQ_TYPE_Q4_K, 144, 8 * GQ_K45_SUB, GQ_K45_STAGES, GQ_K45_WARPS)   // sub-tiles of 8 super-blocks
 GQ_FMT(GQ_TYPE_Q5_K, 176, 8 * GQ_Q5K_SUB, GQ_Q5K_STAGES, 8)
-GQ_FMT(GQ_TYPE_Q6_K, 210, 8, 3, 8)   // 128 blocks of 16 per tile
+GQ_FMT(GQ_TYPE_Q6_K, 210, 8 * GQ_Q6K_SUB, GQ_Q6K_STAGES, 8)   // sub-tiles of 128 blocks of 16
 GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4, 8)   // 32 blocks of 32 per tile
 GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4, 8)
 GQ_FMT(GQ_TYPE_Q4_1, 20, 32, 4, 8)   // 32 blocks of 32 per tile, one per lane
@@ -240,8 +246,8 @@ __device__ __noinline__ gq_diag_t k45_block_exact(const uint8_t* sbp, int g, boo
     float S, M;
     k45_block_constants(sbp, 2 * g + (H ? 1 : 0), S, M);
     const Requant p = requant_block(S, M, qmin, qmax, -128, 127, recip);
-    codes[lane] = static_cast<uint8_t>(requant_value(q, p.sf, p.rm, -128, 127));
-    if (lane == 0) *scale = p.scale;
+    st_global(codes + lane, static_cast<uint8_t>(requant_value(q, p.sf, p.rm, -128, 127)));
+    if (lane == 0) st_global(scale, p.scale);
     gq_diag_t diag;
     diag.round_err_bits = __float_as_uint(p.round_err);
     diag.clip_err = p.clip_err;
@@ -330,7 +336,7 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
         const FastRequant pL = requant_fast(SL, ML, qminL, qmaxL, -128, 127, recip);
         const FastRequant pH = requant_fast(SH, MH, qminH, qmaxH, -128, 127, recip);
         if (valid) {
-            *reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g) = make_float2(pL.scale, pH.scale);
+            st_global(reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g), make_float2(pL.scale, pH.scale));
             acc.add(fmaxf(pL.round_err, pH.round_err), 0);
         }
         constexpr uint32_t kBias = 0x400u;   // lane value q*sf + rm + bias stays in [0, 4096)
@@ -456,7 +462,7 @@ __device__ __forceinline__ void process_q6k(const GqDesc& D, int64_t unit0, int 
         if (MODE & kOutCodes) {
             stg128(D.codes + off, make_uint4(code[0], code[1], code[2], code[3]));
             // block scale f16(f32(sc) * f32(d)) (ggml_quant.py:771-773), no requant (:700)
-            D.scales[ou * 16 + kb] = round_to_f16(__fmul_rn(static_cast<float>(sc), d));
+            st_global(D.scales + ou * 16 + kb, round_to_f16(__fmul_rn(static_cast<float>(sc), d)));
         }
         if (MODE & kOutF32) {
             // gguf-py Q6_K.dequantize_blocks: (d * sc) * q
@@ -483,7 +489,7 @@ __device__ __forceinline__ void process_q0(const GqDesc& D, int64_t unit0, int n
                                            const uint8_t* tile, int lane) {
     constexpr int UB = Q4 ? 18 : 34;
     if ((MODE & kOutCodes) && lane < nunits) {
-        D.scales[permute_unit(D, unit0 + lane)] = h2f(lds16(tile + UB * lane));
+        st_global(D.scales + permute_unit(D, unit0 + lane), h2f(lds16(tile + UB * lane)));
     }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -596,7 +602,7 @@ __device__ __forceinline__ void process_q32(const GqDesc& D, int64_t unit0, int 
             for (int i = 0; i < 8; ++i) c[i] = (q[i] + 0x70707070u) ^ 0x80808080u;
         }
         if (valid) {
-            D.scales[ou] = scale;
+            st_global(D.scales + ou, scale);
             stg128(D.codes + ou * 32, make_uint4(c[0], c[1], c[2], c[3]));
             stg128(D.codes + ou * 32 + 16, make_uint4(c[4], c[5], c[6], c[7]));
         }
@@ -676,13 +682,13 @@ __device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int 
                 for (int i = 0; i < 4; ++i) cw[i] = requant_word(q[i], p);
                 if (valid) {
                     acc.add(p.round_err, p.clip_err);
-                    D.scales[ou * 16 + kb] = p.scale;
+                    st_global(D.scales + ou * 16 + kb, p.scale);
                 }
             } else {
                 // Q3_K: codes q - 4 (per byte, q <= 7: (q + 0x7C) ^ 0x80), scale f16(sc * d)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) cw[i] = (q[i] + 0x7C7C7C7Cu) ^ 0x80808080u;
-                if (valid) D.scales[ou * 16 + kb] = S;
+                if (valid) st_global(D.scales + ou * 16 + kb, S);
             }
             if (valid) stg128(D.codes + ou * 256 + 16 * kb, make_uint4(cw[0], cw[1], cw[2], cw[3]));
         }
@@ -762,7 +768,12 @@ __global__ void __launch_bounds__(Fmt<TYPE>::kThreads,
                                                            tile + 8 * j * F::kUnitBytes, lane, acc, recip);
             }
         } else if (TYPE == GQ_TYPE_Q6_K) {
-            process_q6k<MODE>(D, unit0, nunits, tile, lane);
+#pragma unroll 1
+            for (int j = 0; j < F::kUnitsPerTile / 8; ++j) {
+                const int rest = nunits - 8 * j;
+                if (rest <= 0) break;
+                process_q6k<MODE>(D, unit0 + 8 * j, rest < 8 ? rest : 8, tile + 8 * j * F::kUnitBytes, lane);
+            }
         } else if (TYPE == GQ_TYPE_Q4_1 || TYPE == GQ_TYPE_Q5_0 || TYPE == GQ_TYPE_Q5_1) {
             if (MODE & kOutCodes) acc.retarget(D.diag, lane);
             process_q32<TYPE, MODE>(D, unit0, nunits, tile, lane, acc, recip);
