@@ -27,8 +27,8 @@ from ml_dtypes import bfloat16, int4
 from . import _native as N
 from .formats import FORMAT_BY_ID, FORMATS
 
-__all__ = ["unpack_gguf_tensor", "load_tensor", "convert_host", "GgufReaderProxy", "install",
-           "requant_warning"]
+__all__ = ["unpack_gguf_tensor", "load_tensor", "load_partition", "convert_host", "GgufReaderProxy",
+           "install", "requant_warning"]
 
 # Same logger and text as ggml_quant.py:879-880, so log handling stays as it was.
 _log = logging.getLogger("sima_lmm.gguf.ggml_quant")
@@ -153,6 +153,39 @@ def load_tensor(gguf_tensor, force_float: bool, perm_heads: int = 0):
     if d is not None:
         requant_warning(*d)
     return s, w.reshape(shape)
+
+
+def load_partition(gguf_tensor, count: int, index: int, span: int, force_float: bool = False):
+    """A bundled projection's selected rows, decoded on their own.
+
+    ``_build_conv`` decodes the whole bundled tensor (``qkv_proj``, ``gate_up_proj``) for
+    each projection and keeps the rows ``_get_array_partition(count, index, span)`` selects,
+    from the weights and from the scales reshaped to (rows, blocks per row)
+    (model_graph.py:990-998, 1012-1016, 1168-1195).  GGUF stores rows contiguously, so
+    only the selected rows' bytes are converted here.  Returns (scales | None, weights) for
+    those rows: scales (selected blocks, 1) in row order and weights (r1 - r0, ...), i.e.
+    the partition of ``unpack_gguf_tensor``'s result.  The requantization warning then
+    covers the decoded rows only."""
+    from .layout import array_partition
+
+    name = _type_name(gguf_tensor.tensor_type)
+    shape = tuple(int(x) for x in gguf_tensor.shape[::-1])
+    r0, r1 = array_partition(shape[0], count, index, span)
+    if name in ("F32", "F16", "BF16"):
+        s, w = load_tensor(gguf_tensor, force_float, 0)
+        return None, w[r0:r1]
+    if name == "Q8_1" and not force_float:
+        raise KeyError("Q8_1")
+    if name not in _GPU_TYPES:
+        raise NotImplementedError(f"GGML type {name} is not handled by the B200 GGUF path")
+    f = FORMATS[name]
+    cols = int(np.prod(shape[1:])) if len(shape) > 1 else 1
+    row_bytes = cols // f.unit_values * f.unit_bytes
+    raw = np.asarray(gguf_tensor.data).reshape(-1).view(np.uint8)[r0 * row_bytes:r1 * row_bytes]
+    s, w, d = convert_host(name, raw, r1 - r0, cols, force_float)
+    if d is not None:
+        requant_warning(*d)
+    return s, w.reshape((r1 - r0, *shape[1:]))
 
 
 def unpack_gguf_tensor(gguf_tensor, force_float: bool):

@@ -103,6 +103,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--out", default=str(HERE))
+    ap.add_argument("--only", choices=["all", "partition"], default="all",
+                    help="partition: rewrite only partition.json")
     args = ap.parse_args()
 
     sys.path.insert(0, args.reference)
@@ -146,49 +148,80 @@ def main():
         manifest.append({"case": case, "fmt": fmt, "rows": rows, "cols": cols,
                          "heads": heads, "warning": bool(warning)})
 
-    shapes = {"Q8_0": [(37, 64), (6, 4096)], "Q4_0": [(37, 64), (6, 4096)],
-              "Q4_K": [(37, 256), (5, 4096)], "Q5_K": [(37, 256), (5, 4096)],
-              "Q6_K": [(37, 256), (5, 4096)],
-              "Q4_1": [(37, 64), (6, 1024)], "Q5_0": [(37, 64), (6, 1024)],
-              "Q5_1": [(37, 64), (6, 1024)], "Q2_K": [(37, 256), (3, 2048)],
-              "Q3_K": [(37, 256), (3, 2048)]}
-    for fmt, shp in shapes.items():
-        for seed in (0, 1, 2):
-            for rows, cols in shp:
-                raw = gen_tensor_bytes(fmt, rows * cols, 1000 * seed + rows)
-                run(f"{fmt}_seed{seed}_{rows}x{cols}", fmt, raw, rows, cols)
-        run(f"{fmt}_single_unit", fmt, gen_tensor_bytes(fmt, FORMATS[fmt].unit_values, 77),
-            1, FORMATS[fmt].unit_values)
-        run(f"{fmt}_nonfinite", fmt, _nonfinite(fmt, 96 if FORMATS[fmt].unit_values == 256 else 384, 5),
-            12 if FORMATS[fmt].unit_values == 256 else 48, 2048 if FORMATS[fmt].unit_values == 256 else 256)
-    for fmt in ("Q4_K", "Q5_K", "Q6_K"):
-        run(f"{fmt}_edges", fmt, _edge_kquant(fmt, 96, 11), 24, 1024)
-    run("Q2_K_perm_q", "Q2_K", gen_tensor_bytes("Q2_K", 32 * 512, 25), 32, 512, heads=2)
-    # q/k head permutation of a llama-style model: 4 heads of dim 16, and 2 kv heads
-    run("Q4_K_perm_q", "Q4_K", gen_tensor_bytes("Q4_K", 64 * 512, 21), 64, 512, heads=4)
-    run("Q6_K_perm_k", "Q6_K", gen_tensor_bytes("Q6_K", 32 * 512, 22), 32, 512, heads=2)
-    run("Q8_0_perm_q", "Q8_0", gen_tensor_bytes("Q8_0", 64 * 128, 23), 64, 128, heads=4)
-    run("F32_norm", "F32", gen_tensor_bytes("F32", 1000, 24, "norm"), 1000, 1)
-
-    # Modalix layout: the reference's own _layout_array (model_graph.py:1271-1304), taken
-    # from the source file (the module imports the absent afe SDK), applied as
-    # _build_conv does (model_graph.py:1012-1042)
     import ast
     src_path = Path(args.reference) / "sima_lmm" / "model" / "model_graph.py"
     tree = ast.parse(src_path.read_text())
-    fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "_layout_array")
-    ns: dict = {"np": np}
-    exec(compile(ast.Module(body=[fn], type_ignores=[]), str(src_path), "exec"), ns)
-    layout_array = ns["_layout_array"]
-    for case, (out_ch, in_ch, block) in {"layout_97x96": (97, 96, 32), "layout_64x512": (64, 512, 16)}.items():
-        rng = np.random.default_rng(out_ch)
-        codes = rng.integers(-128, 128, size=(out_ch, in_ch), dtype=np.int8)
-        scales = rng.random((out_ch * in_ch // block, 1), dtype=np.float32)
-        sc = np.transpose(np.reshape(scales, (codes.shape[0], -1)), axes=[1, 0])
-        w = layout_array(layout_array(codes, "oi", "oihw"), "oihw", "hwigo")
-        np.savez_compressed(out / f"{case}.npz", codes=codes, scales=scales, out_scales=sc, out_weight=w,
-                            block=block, kind="layout")
-        manifest.append({"case": case, "fmt": "layout", "rows": out_ch, "cols": in_ch})
+    if args.only == "all":
+        shapes = {"Q8_0": [(37, 64), (6, 4096)], "Q4_0": [(37, 64), (6, 4096)],
+                  "Q4_K": [(37, 256), (5, 4096)], "Q5_K": [(37, 256), (5, 4096)],
+                  "Q6_K": [(37, 256), (5, 4096)],
+                  "Q4_1": [(37, 64), (6, 1024)], "Q5_0": [(37, 64), (6, 1024)],
+                  "Q5_1": [(37, 64), (6, 1024)], "Q2_K": [(37, 256), (3, 2048)],
+                  "Q3_K": [(37, 256), (3, 2048)]}
+        for fmt, shp in shapes.items():
+            for seed in (0, 1, 2):
+                for rows, cols in shp:
+                    raw = gen_tensor_bytes(fmt, rows * cols, 1000 * seed + rows)
+                    run(f"{fmt}_seed{seed}_{rows}x{cols}", fmt, raw, rows, cols)
+            run(f"{fmt}_single_unit", fmt, gen_tensor_bytes(fmt, FORMATS[fmt].unit_values, 77),
+                1, FORMATS[fmt].unit_values)
+            run(f"{fmt}_nonfinite", fmt, _nonfinite(fmt, 96 if FORMATS[fmt].unit_values == 256 else 384, 5),
+                12 if FORMATS[fmt].unit_values == 256 else 48, 2048 if FORMATS[fmt].unit_values == 256 else 256)
+        for fmt in ("Q4_K", "Q5_K", "Q6_K"):
+            run(f"{fmt}_edges", fmt, _edge_kquant(fmt, 96, 11), 24, 1024)
+        run("Q2_K_perm_q", "Q2_K", gen_tensor_bytes("Q2_K", 32 * 512, 25), 32, 512, heads=2)
+        # q/k head permutation of a llama-style model: 4 heads of dim 16, and 2 kv heads
+        run("Q4_K_perm_q", "Q4_K", gen_tensor_bytes("Q4_K", 64 * 512, 21), 64, 512, heads=4)
+        run("Q6_K_perm_k", "Q6_K", gen_tensor_bytes("Q6_K", 32 * 512, 22), 32, 512, heads=2)
+        run("Q8_0_perm_q", "Q8_0", gen_tensor_bytes("Q8_0", 64 * 128, 23), 64, 128, heads=4)
+        run("F32_norm", "F32", gen_tensor_bytes("F32", 1000, 24, "norm"), 1000, 1)
+
+        # Modalix layout: the reference's own _layout_array (model_graph.py:1271-1304), taken
+        # from the source file (the module imports the absent afe SDK), applied as
+        # _build_conv does (model_graph.py:1012-1042)
+        fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "_layout_array")
+        ns: dict = {"np": np}
+        exec(compile(ast.Module(body=[fn], type_ignores=[]), str(src_path), "exec"), ns)
+        layout_array = ns["_layout_array"]
+        for case, (out_ch, in_ch, block) in {"layout_97x96": (97, 96, 32), "layout_64x512": (64, 512, 16)}.items():
+            rng = np.random.default_rng(out_ch)
+            codes = rng.integers(-128, 128, size=(out_ch, in_ch), dtype=np.int8)
+            scales = rng.random((out_ch * in_ch // block, 1), dtype=np.float32)
+            sc = np.transpose(np.reshape(scales, (codes.shape[0], -1)), axes=[1, 0])
+            w = layout_array(layout_array(codes, "oi", "oihw"), "oihw", "hwigo")
+            np.savez_compressed(out / f"{case}.npz", codes=codes, scales=scales, out_scales=sc, out_weight=w,
+                                block=block, kind="layout")
+            manifest.append({"case": case, "fmt": "layout", "rows": out_ch, "cols": in_ch})
+
+    # Bundled projections: the reference's own ModelGraph._find_alternate_weight and
+    # _get_array_partition (model_graph.py:1168-1248), taken from the class body the same
+    # way, applied to a row-index array
+    cls = next(n for n in tree.body if isinstance(n, ast.ClassDef) and n.name == "ModelGraph")
+    fns = [n for n in cls.body if isinstance(n, ast.FunctionDef)
+           and n.name in ("_get_array_partition", "_find_alternate_weight")]
+    pns: dict = {"np": np, "Callable": object}
+    for fn_def in fns:
+        fn_def.decorator_list = []   # plain functions; _find_alternate_weight names ModelGraph
+    exec(compile(ast.Module(body=fns, type_ignores=[]), str(src_path), "exec"), pns)
+    mgc = types.SimpleNamespace(**{f.name: pns[f.name] for f in fns})
+    pns["ModelGraph"] = mgc
+    part_cases = []
+    for wname, q_size, kv_size, rows in [
+            ("model.layers.0.self_attn.q_proj.weight", 32, 32, 9216),
+            ("model.layers.0.self_attn.k_proj.weight", 32, 32, 9216),
+            ("model.layers.0.self_attn.v_proj.weight", 32, 32, 9216),
+            ("model.layers.3.self_attn.q_proj.weight", 24, 8, 5120),
+            ("model.layers.3.self_attn.k_proj.weight", 24, 8, 5120),
+            ("model.layers.3.self_attn.v_proj.weight", 24, 8, 5120),
+            ("model.layers.1.mlp.gate_proj.weight", None, None, 16384),
+            ("model.layers.1.mlp.up_proj.weight", None, None, 16384)]:
+        fused, fn = mgc._find_alternate_weight(wname, q_size, kv_size)
+        kept = fn(np.arange(rows))
+        part_cases.append({"weight": wname, "q_size": q_size, "kv_size": kv_size, "rows": rows,
+                           "fused": fused, "r0": int(kept[0]), "r1": int(kept[-1]) + 1})
+    (out / "partition.json").write_text(json.dumps(part_cases, indent=1) + "\n")
+    if args.only == "partition":
+        return
 
     versions = {"numpy": np.__version__, "ml_dtypes": ml_dtypes.__version__,
                 "gguf": getattr(gguf, "__version__", None) or _dist_version("gguf"),

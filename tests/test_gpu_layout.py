@@ -60,3 +60,62 @@ def test_layout_against_reference_layout_array_golden():
         with np.load(GOLDEN / f"{name}.npz") as z:
             s, w = modalix_layout(z["scales"], z["codes"])
             assert np.array_equal(w, z["out_weight"]) and np.array_equal(s, z["out_scales"])
+
+
+@pytest.mark.parametrize("fmt,q_size,kv_size,element", [("Q4_K", 4, 2, 8), ("Q6_K", 3, 1, 16), ("Q8_0", 4, 4, 2),
+                                                        ("Q4_0", 2, 1, 16), ("Q5_K", 4, 2, 4)])
+def test_bundled_qkv_rows_decoded_on_their_own(fmt, q_size, kv_size, element):
+    # load_partition(qkv_proj, ...) == _get_array_partition applied to the full decode
+    # (model_graph.py:990-998, 1012-1016, 1168-1248), weights and reshaped scales
+    import types
+
+    from llima_b200.formats import FORMATS
+    from llima_b200.gguf_conversion import load_partition
+    from llima_b200.layout import alternate_weight, array_partition
+    from llima_b200.synth import gen_tensor_bytes
+
+    f = FORMATS[fmt]
+    rows, cols = (q_size + 2 * kv_size) * element, 2 * f.unit_values
+    raw = gen_tensor_bytes(fmt, rows * cols, rows + cols)
+    tensor = types.SimpleNamespace(tensor_type=f.type_id, data=raw.reshape(rows, -1),
+                                   shape=np.array([cols, rows], dtype=np.uint64))
+    full_s, full_w, _ = O.unpack_tensor(fmt, raw, (rows, cols), log=False)
+    for proj in ("q_proj", "k_proj", "v_proj"):
+        fused, count, index, span = alternate_weight(f"blk.0.self_attn.{proj}.weight", q_size, kv_size)
+        assert fused == "blk.0.self_attn.qkv_proj.weight"
+        r0, r1 = array_partition(rows, count, index, span)
+        s, w = load_partition(tensor, count, index, span)
+        assert w.shape == (r1 - r0, cols)
+        assert np.array_equal(np.asarray(w).view(np.uint8), np.asarray(full_w[r0:r1]).view(np.uint8))
+        want_s = np.reshape(full_s, (rows, -1))[r0:r1]
+        assert np.array_equal(np.reshape(s, want_s.shape).view(np.uint32), want_s.view(np.uint32))
+        _, v = load_partition(tensor, count, index, span, force_float=True)
+        full_f = O.gguf_dequantize(raw, fmt).reshape(rows, cols)
+        assert np.array_equal(v.view(np.uint32), full_f[r0:r1].view(np.uint32))
+
+
+def test_bundled_gate_up_and_float_tensors():
+    import types
+
+    from llima_b200.formats import FORMATS
+    from llima_b200.gguf_conversion import load_partition
+    from llima_b200.layout import alternate_weight
+    from llima_b200.synth import gen_tensor_bytes
+
+    rows, cols = 48, 512
+    raw = gen_tensor_bytes("Q4_K", rows * cols, 9)
+    tensor = types.SimpleNamespace(tensor_type=FORMATS["Q4_K"].type_id, data=raw.reshape(rows, -1),
+                                   shape=np.array([cols, rows], dtype=np.uint64))
+    full_s, full_w, _ = O.unpack_tensor("Q4_K", raw, (rows, cols), log=False)
+    for proj, (r0, r1) in (("gate_proj", (0, 24)), ("up_proj", (24, 48))):
+        fused, count, index, span = alternate_weight(f"blk.2.mlp.{proj}.weight", None, None)
+        assert fused == "blk.2.mlp.gate_up_proj.weight"
+        s, w = load_partition(tensor, count, index, span)
+        assert np.array_equal(w, full_w[r0:r1])
+        assert np.array_equal(np.reshape(s, (24, -1)), np.reshape(full_s, (rows, -1))[r0:r1])
+    bias = np.random.default_rng(3).normal(0, 0.02, 96).astype(np.float32)
+    bt = types.SimpleNamespace(tensor_type=FORMATS["F32"].type_id, data=bias, shape=np.array([96], dtype=np.uint64))
+    s, b = load_partition(bt, 6, 2, 2)
+    assert s is None and np.array_equal(b, bias[32:64])
+    with pytest.raises(AssertionError):
+        load_partition(bt, 7, 0, 1)
