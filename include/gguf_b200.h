@@ -26,6 +26,9 @@
  *   gq_requantize_symmetric         sima_lmm/gguf/ggml_quant.py:785-886 (requantize_symmetric)
  *   gq_query                        sizes implied by ggml_quant.py:104-131 (format table)
  *   gq_convert_host                 the same as gq_convert_batch, on host buffers
+ *   gq_unpack_fields                sima_lmm/gguf/ggml_quant.py:567-694 (unpack_k_quant) and
+ *                                   :174-271 (unpack_q4 / unpack_q5, ASYMMETRIC)
+ *   gq_remove_superblocks           sima_lmm/gguf/ggml_quant.py:739-782 (remove_superblocks)
  *
  * Conventions: every function returns GQ_OK (0) or a negative GQ_ERR_* code and never
  * aborts; gq_strerror() describes a code.  Device pointers are plain CUDA device
@@ -153,6 +156,32 @@ GQ_API int gq_requantize_symmetric(const float* block_consts, const int8_t* code
 GQ_API int gq_modalix_layout(const void* codes, const float* scales, int64_t rows, int64_t cols,
                              int32_t block_values, int64_t rows_padded, void* out_codes, float* out_scales,
                              void* stream);
+
+/* The field-level steps of the reference's ggml_quant module, for callers that use them
+ * one by one (the conversion entry points above fuse them).
+ *
+ * gq_unpack_fields: unpack_k_quant (sima_lmm/gguf/ggml_quant.py:567-694) for Q2_K, Q3_K,
+ * Q4_K, Q5_K and Q6_K, and the ASYMMETRIC branches of unpack_q4 / unpack_q5
+ * (ggml_quant.py:174-271) for Q4_1 / Q5_1.  Splits n_units stored units into their fields
+ * with no arithmetic beyond widening the f16 constants to f32:
+ *   K-quants: super_consts (n_units, k) f32 (k = 2: d, dmin for Q2_K / Q4_K / Q5_K;
+ *             k = 1: d), block_consts (n_units, B, k) int8 (B = 8 for Q4_K / Q5_K, else
+ *             16), values (n_units, B, 256 / B) int8 (Q3_K and Q6_K already offset by
+ *             -4 / -32, the others unsigned).
+ *   Q4_1 / Q5_1: super_consts receives the block constants (n_units, 2) f32 [d, m];
+ *             block_consts must be NULL; values (n_units, 32): 0..15 / 0..31.
+ * Device pointers: src and values 16-byte aligned, super_consts and block_consts 8. */
+GQ_API int gq_unpack_fields(int32_t type, const void* src, size_t src_bytes, int64_t n_units,
+                            float* super_consts, int8_t* block_consts, int8_t* values, void* stream);
+
+/* remove_superblocks (ggml_quant.py:739-782): out[i*B + b, c] = f16(f32(block_consts[i, b, c]) *
+ * super_consts[i, c]) (one f32 product, then round-to-nearest-even to f16), negated for
+ * c = 1 when n_consts = 2 (the min).  block_consts are int8 (block_elem_bytes 1) or int16
+ * (2); outputs (n_super * B, n_consts) as f16 bit patterns and / or their f32 widening
+ * (either output may be NULL, not both).  Device pointers. */
+GQ_API int gq_remove_superblocks(const float* super_consts, const void* block_consts, int32_t block_elem_bytes,
+                                 int64_t n_super, int32_t blocks_per_super, int32_t n_consts,
+                                 uint16_t* out_f16, float* out_f32, void* stream);
 
 /* Token embeddings for the on-device runtime: LanguageModel.get_embeddings_tensor
  * (sima_lmm/model/language_model.py:578-611) fused with quantize_embedding_rows (:38-54).

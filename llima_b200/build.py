@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libgguf_b200.so"
-SOURCES = ["gq_kernels.cu", "gq_embed.cu", "gq_layout.cu", "gq_api.cu"]
+SOURCES = ["gq_kernels.cu", "gq_embed.cu", "gq_layout.cu", "gq_fields.cu", "gq_api.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

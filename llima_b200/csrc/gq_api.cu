@@ -245,6 +245,41 @@ int gq_requantize_symmetric(const float* block_consts, const int8_t* codes, int6
                                           out_codes, diag, stream));
 }
 
+int gq_unpack_fields(int32_t type, const void* src, size_t src_bytes, int64_t n_units, float* super_consts,
+                     int8_t* block_consts, int8_t* values, void* stream) {
+    TypeInfo ti;
+    if (!type_info(type, &ti)) return GQ_ERR_TYPE;
+    const bool kq = ti.unit_values == 256;
+    if (!kq && type != GQ_TYPE_Q4_1 && type != GQ_TYPE_Q5_1) return GQ_ERR_TYPE;
+    if (n_units < 0 || n_units > INT64_MAX / 256) return GQ_ERR_SIZE;
+    if (static_cast<uint64_t>(n_units) * ti.unit_bytes > src_bytes) return GQ_ERR_SIZE;
+    if (n_units == 0) return GQ_OK;
+    if (src == nullptr || super_consts == nullptr || values == nullptr) return GQ_ERR_NULL;
+    if (kq != (block_consts != nullptr)) return block_consts ? GQ_ERR_ARG : GQ_ERR_NULL;
+    if (!aligned(src, 16) || !aligned(values, 16) || !aligned(super_consts, 8) ||
+        (block_consts && !aligned(block_consts, 8)))
+        return GQ_ERR_ALIGN;
+    return cuda_status(gq::launch_fields(type, static_cast<const uint8_t*>(src), n_units, super_consts,
+                                         block_consts, values, stream));
+}
+
+int gq_remove_superblocks(const float* super_consts, const void* block_consts, int32_t block_elem_bytes,
+                          int64_t n_super, int32_t blocks_per_super, int32_t n_consts, uint16_t* out_f16,
+                          float* out_f32, void* stream) {
+    if (block_elem_bytes != 1 && block_elem_bytes != 2) return GQ_ERR_ARG;
+    if (n_consts != 1 && n_consts != 2) return GQ_ERR_ARG;
+    if (n_super < 0 || blocks_per_super < 1 || n_super > INT64_MAX / (2 * int64_t(blocks_per_super)))
+        return GQ_ERR_SIZE;
+    if (n_super == 0) return GQ_OK;
+    if (super_consts == nullptr || block_consts == nullptr || (out_f16 == nullptr && out_f32 == nullptr))
+        return GQ_ERR_NULL;
+    if (!aligned(super_consts, 4) || !aligned(block_consts, block_elem_bytes) || !aligned(out_f16, 2) ||
+        !aligned(out_f32, 4))
+        return GQ_ERR_ALIGN;
+    return cuda_status(gq::launch_superblocks(super_consts, block_consts, block_elem_bytes, n_super,
+                                              blocks_per_super, n_consts, out_f16, out_f32, stream));
+}
+
 int gq_modalix_layout(const void* codes, const float* scales, int64_t rows, int64_t cols, int32_t block_values,
                       int64_t rows_padded, void* out_codes, float* out_scales, void* stream) {
     if (rows < 0 || cols < 0 || rows_padded < rows) return GQ_ERR_SIZE;

@@ -60,5 +60,10 @@ int launch_embed(int type, bool from_f32, const uint8_t* src, int64_t rows, int6
                  void* stream);
 int launch_requant(const float* bc, const int8_t* codes, int64_t n_blocks, int block, int bits,
                    float* out_scales, int8_t* out_codes, gq_diag_t* diag, void* stream);
+// implemented in gq_fields.cu
+int launch_fields(int type, const uint8_t* src, int64_t n_units, float* sup, int8_t* blk, int8_t* vals,
+                  void* stream);
+int launch_superblocks(const float* sup, const void* blk, int blk_bytes, int64_t n_super, int nb, int k,
+                       uint16_t* out_f16, float* out_f32, void* stream);
 
 }  // namespace gq

@@ -103,8 +103,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--out", default=str(HERE))
-    ap.add_argument("--only", choices=["all", "partition"], default="all",
-                    help="partition: rewrite only partition.json")
+    ap.add_argument("--only", choices=["all", "partition", "ggml_quant"], default="all",
+                    help="partition: rewrite only partition.json; ggml_quant: only ggml_quant/*.npz")
     args = ap.parse_args()
 
     sys.path.insert(0, args.reference)
@@ -119,6 +119,10 @@ def main():
     logging.getLogger("sima_lmm.gguf.ggml_quant").addHandler(cap)
     out = Path(args.out)
     manifest = []
+    if args.only == "ggml_quant":
+        from sima_lmm.gguf import ggml_quant as gq
+        write_ggml_quant(gq, cap, out / "ggml_quant", ml_dtypes, gguf)
+        return
 
     def run(case: str, fmt: str, raw: np.ndarray, rows: int, cols: int, heads: int = 0):
         f = FORMATS[fmt]
@@ -228,6 +232,79 @@ def main():
                 "reference": "sima-neat/llima 0.6.2", "cases": manifest}
     (out / "versions.json").write_text(json.dumps(versions, indent=1) + "\n")
     print(f"wrote {len(manifest)} cases to {out}")
+
+
+def write_ggml_quant(gq, cap, out: Path, ml_dtypes, gguf):
+    """Golden vectors of the reference's function-level ggml_quant API
+    (``ggml_quant.py:136-886``): every unpacker, ``remove_superblocks``,
+    ``convert_to_simple_block_quant`` and ``requantize_symmetric`` on seeded bytes (with
+    the BASELINE distributions) and on uniform random bytes (NaN / inf / huge f16
+    constants), each function's outputs stored under its own name."""
+    out.mkdir(exist_ok=True)
+    sym, asym = gq.QuantizationSymmetry.SYMMETRIC, gq.QuantizationSymmetry.ASYMMETRIC
+    cases = []
+
+    def u8(a):
+        return a.view(np.uint8) if a.dtype in (ml_dtypes.int4, ml_dtypes.uint4) else a
+
+    def call(rec, key, fn, *a):
+        cap.messages.clear()
+        with np.errstate(all="ignore"):
+            res = fn(*a)
+        rec[f"{key}__warning"] = "\n".join(cap.messages)
+        if not isinstance(res, tuple):
+            res = (res,)
+        for i, r in enumerate(res):
+            if r is not None:
+                rec[f"{key}__{i}"] = u8(r)
+                rec[f"{key}__{i}__dtype"] = str(r.dtype)
+        return res
+
+    for fmt in ("Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"):
+        f = FORMATS[fmt]
+        n_units = 37 if f.unit_values == 256 else 296
+        for kind in ("seed0", "seed1", "random"):
+            if kind == "random":
+                raw = _nonfinite(fmt, n_units, 99)
+            else:
+                raw = gen_tensor_bytes(fmt, n_units * f.unit_values, 500 + int(kind[-1]) * 7 + f.type_id)
+            data = raw.tobytes()
+            rec = {"raw": raw, "fmt": fmt}
+            if fmt == "Q8_0":
+                call(rec, "unpack_q8_0", gq.unpack_q8_0, data)
+                call(rec, "unpack_dequantize_q8_0", gq.unpack_dequantize_q8_0, data)
+                call(rec, "unpack_base_quant", gq.unpack_base_quant, data, fmt)
+            elif fmt in ("Q4_0", "Q4_1"):
+                s = sym if fmt == "Q4_0" else asym
+                c, w = call(rec, "unpack_q4", gq.unpack_q4, data, s)
+                call(rec, "unpack_dequantize_q4", gq.unpack_dequantize_q4, data, s)
+                call(rec, "unpack_base_quant", gq.unpack_base_quant, data, fmt)
+                if fmt == "Q4_1":
+                    call(rec, "requantize_symmetric_8", gq.requantize_symmetric, c, w, 8, np.int8)
+                    call(rec, "requantize_symmetric_4", gq.requantize_symmetric, c, w, 4, np.int16)
+            elif fmt in ("Q5_0", "Q5_1"):
+                s = sym if fmt == "Q5_0" else asym
+                c, w = call(rec, "unpack_q5", gq.unpack_q5, data, s)
+                call(rec, "unpack_base_quant", gq.unpack_base_quant, data, fmt)
+                if fmt == "Q5_1":
+                    call(rec, "requantize_symmetric_8", gq.requantize_symmetric, c, w, 8, np.int8)
+                    call(rec, "requantize_symmetric_6", gq.requantize_symmetric, c, w, 6, np.int8)
+            else:
+                sup, blk, vals = call(rec, "unpack_k_quant", gq.unpack_k_quant, data, fmt)
+                bc, q = call(rec, "remove_superblocks", gq.remove_superblocks, sup, blk, vals)
+                call(rec, "remove_superblocks_f16_i16", gq.remove_superblocks, sup.astype(np.float16),
+                     blk.astype(np.int16), vals)
+                call(rec, "convert_to_simple_block_quant", gq.convert_to_simple_block_quant, sup, blk, vals)
+                if bc.shape[1] == 2:
+                    call(rec, "requantize_symmetric_5", gq.requantize_symmetric, bc.astype(np.float32), q, 5,
+                         np.int32)
+            np.savez_compressed(out / f"{fmt}_{kind}.npz", **rec)
+            cases.append(f"{fmt}_{kind}")
+    versions = {"numpy": np.__version__, "ml_dtypes": ml_dtypes.__version__,
+                "gguf": getattr(gguf, "__version__", None) or _dist_version("gguf"),
+                "reference": "sima-neat/llima 0.6.2", "cases": cases}
+    (out / "versions.json").write_text(json.dumps(versions, indent=1) + "\n")
+    print(f"wrote {len(cases)} ggml_quant cases to {out}")
 
 
 def _dist_version(name: str):

@@ -57,6 +57,19 @@ def test_validation_errors_before_any_cuda_call():
     assert lib.gq_convert_batch(None, 0, 1, None) == 0
     assert lib.gq_requantize_symmetric(None, None, 1, 0, 8, None, None, None, None) == -5
     assert lib.gq_requantize_symmetric(None, None, 1, 32, 9, None, None, None, None) == -5
+    # field unpack: types off its list, sizes, NULL / misaligned pointers, no CUDA call
+    assert lib.gq_unpack_fields(8, None, 0, 1, None, None, None, None) == -1         # Q8_0
+    assert lib.gq_unpack_fields(12, None, 143, 1, None, None, None, None) == -2      # too few bytes
+    assert lib.gq_unpack_fields(12, None, 0, 0, None, None, None, None) == 0         # empty
+    assert lib.gq_unpack_fields(12, None, 144, 1, None, None, None, None) == -4
+    assert lib.gq_unpack_fields(12, 0x1000, 144, 1, 0x2000, None, 0x3000, None) == -4   # K needs blk
+    assert lib.gq_unpack_fields(3, 0x1000, 20, 1, 0x2000, 0x4000, 0x3000, None) == -5   # Q4_1 has none
+    assert lib.gq_unpack_fields(12, 0x1008, 144, 1, 0x2000, 0x4000, 0x3000, None) == -3
+    assert lib.gq_remove_superblocks(None, None, 4, 1, 8, 2, None, None, None) == -5
+    assert lib.gq_remove_superblocks(None, None, 1, 1, 8, 3, None, None, None) == -5
+    assert lib.gq_remove_superblocks(None, None, 1, 0, 8, 2, None, None, None) == 0
+    assert lib.gq_remove_superblocks(0x1000, 0x2000, 1, 1, 8, 2, None, None, None) == -4
+    assert lib.gq_remove_superblocks(0x1002, 0x2000, 1, 1, 8, 2, 0x3000, None, None) == -3
 
 
 def test_format_table_matches_oracle():
