@@ -3,10 +3,14 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
+#include <condition_variable>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
 #include <new>
+#include <thread>
 #include <vector>
 
 #include "gq_internal.h"
@@ -337,15 +341,142 @@ int gq_quantize_rows(const float* x, int64_t rows, int64_t cols, int8_t* codes, 
 
 // ---------------------------------------------------------------------------------------
 // Host-buffer session
+//
+// A request is cut into pieces of about kPieceTarget bytes of device footprint (input +
+// outputs; a permuted tensor stays whole), and the pieces rotate through kSlots device
+// slots, each with its own stream.  Pinned host buffers are copied by the DMA engines
+// directly.  A pageable one (a numpy array, the memory map of a GGUF file) is bounced
+// through a pinned host slot laid out like the device slot: a pool of host threads copies
+// the piece's input into it, the GPU copies it in, converts and copies the results back to
+// it, and the pool copies them to the caller's buffers.  While the GPU works on piece p the
+// host drains piece p - 1 and fills piece p + 1, so the host copies, both PCIe directions
+// and the kernels overlap, within one tensor as well as across tensors.
 // ---------------------------------------------------------------------------------------
+
+namespace {
+
+constexpr int kSlots = 3;
+constexpr size_t kPieceTarget = size_t(32) << 20;
+constexpr size_t kCopyChunk = size_t(2) << 20;
+
+struct CopyJob {
+    void* dst;
+    const void* src;
+    size_t bytes;
+};
+
+// Host threads that split a list of copies into chunks and run them together with the
+// calling thread.  Pageable destinations are first touched here, so their page faults
+// are taken in parallel too.
+class CopyPool {
+  public:
+    explicit CopyPool(int threads) {
+        for (int i = 1; i < threads; ++i) workers_.emplace_back([this] { work(); });
+    }
+    ~CopyPool() {
+        {
+            std::lock_guard<std::mutex> g(mu_);
+            stop_ = true;
+        }
+        cv_.notify_all();
+        for (auto& t : workers_) t.join();
+    }
+    void run(const std::vector<CopyJob>& jobs) {
+        auto b = std::make_shared<Batch>();
+        for (const CopyJob& j : jobs)
+            for (size_t o = 0; o < j.bytes; o += kCopyChunk)
+                b->chunks.push_back({static_cast<uint8_t*>(j.dst) + o, static_cast<const uint8_t*>(j.src) + o,
+                                     std::min(kCopyChunk, j.bytes - o)});
+        if (b->chunks.empty()) return;
+        b->left.store(b->chunks.size());
+        if (!workers_.empty() && b->chunks.size() > 1) {
+            {
+                std::lock_guard<std::mutex> g(mu_);
+                current_ = b;
+                ++gen_;
+            }
+            cv_.notify_all();
+        }
+        copy(*b);
+        std::unique_lock<std::mutex> g(b->mu);
+        b->cv.wait(g, [&] { return b->left.load() == 0; });
+    }
+
+  private:
+    struct Batch {
+        std::vector<CopyJob> chunks;
+        std::atomic<size_t> next{0};
+        std::atomic<size_t> left{0};
+        std::mutex mu;
+        std::condition_variable cv;
+    };
+    static void copy(Batch& b) {
+        for (;;) {
+            const size_t i = b.next.fetch_add(1);
+            if (i >= b.chunks.size()) return;
+            std::memcpy(b.chunks[i].dst, b.chunks[i].src, b.chunks[i].bytes);
+            if (b.left.fetch_sub(1) == 1) {
+                std::lock_guard<std::mutex> g(b.mu);
+                b.cv.notify_all();
+            }
+        }
+    }
+    void work() {
+        uint64_t seen = 0;
+        for (;;) {
+            std::shared_ptr<Batch> b;
+            {
+                std::unique_lock<std::mutex> g(mu_);
+                cv_.wait(g, [&] { return stop_ || gen_ != seen; });
+                if (stop_) return;
+                seen = gen_;
+                b = current_;
+            }
+            if (b) copy(*b);
+        }
+    }
+    std::vector<std::thread> workers_;
+    std::mutex mu_;
+    std::condition_variable cv_;
+    std::shared_ptr<Batch> current_;
+    uint64_t gen_ = 0;
+    bool stop_ = false;
+};
+
+int copy_threads() {
+    if (const char* e = std::getenv("LLIMA_B200_COPY_THREADS")) {
+        const int n = std::atoi(e);
+        if (n >= 1) return std::min(n, 64);
+    }
+    const int hw = static_cast<int>(std::thread::hardware_concurrency());
+    return std::max(1, std::min(8, hw / 2));
+}
+
+// A host pointer the DMA engines cannot read or write directly (not pinned or registered).
+bool pageable(const void* p) {
+    if (p == nullptr) return false;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return true;
+    }
+    return a.type != cudaMemoryTypeHost && a.type != cudaMemoryTypeManaged;
+}
+
+}  // namespace
 
 struct gq_session {
     int device = 0;
     size_t slot_bytes = 0;
-    uint8_t* slot[2] = {nullptr, nullptr};
-    cudaStream_t stream[2] = {nullptr, nullptr};
+    uint8_t* slot[kSlots] = {};
+    uint8_t* pinned[kSlots] = {};   // host bounce slots, allocated on first pageable use
+    bool pinned_failed = false;
+    cudaStream_t stream[kSlots] = {};
+    cudaEvent_t done[kSlots] = {};
     gq_diag_t* d_diag = nullptr;
     int diag_cap = 0;
+    std::unique_ptr<CopyPool> pool;
+    std::mutex mu;                  // one gq_convert_host at a time per session
 };
 
 namespace {
@@ -376,6 +507,28 @@ int guard_device(int device) {
     return GQ_OK;
 }
 
+// Pinned bounce slots and the copy pool, on the first request with a pageable buffer.
+// Without them (pinned allocation refused) pageable buffers are handed to the copy
+// engines as they are.
+bool ensure_bounce(gq_session* s) {
+    if (s->pinned[0] != nullptr) return true;
+    if (s->pinned_failed) return false;
+    for (int k = 0; k < kSlots; ++k) {
+        if (cudaHostAlloc(reinterpret_cast<void**>(&s->pinned[k]), s->slot_bytes, cudaHostAllocDefault) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            for (int j = 0; j < kSlots; ++j) {
+                if (s->pinned[j]) cudaFreeHost(s->pinned[j]);
+                s->pinned[j] = nullptr;
+            }
+            s->pinned_failed = true;
+            return false;
+        }
+    }
+    if (!s->pool) s->pool.reset(new (std::nothrow) CopyPool(copy_threads()));
+    return s->pool != nullptr;
+}
+
 }  // namespace
 
 int gq_session_create(int32_t device, size_t staging_bytes, gq_session_t** out) {
@@ -388,13 +541,14 @@ int gq_session_create(int32_t device, size_t staging_bytes, gq_session_t** out) 
     if (!s) return GQ_ERR_NOMEM;
     s->device = device;
     s->slot_bytes = staging_bytes & ~(kAlign - 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kSlots; ++i) {
         if (cudaMalloc(&s->slot[i], s->slot_bytes) != cudaSuccess) {
             gq_session_destroy(s.release());
             cudaGetLastError();
             return GQ_ERR_NOMEM;
         }
-        if (cudaStreamCreateWithFlags(&s->stream[i], cudaStreamNonBlocking) != cudaSuccess) {
+        if (cudaStreamCreateWithFlags(&s->stream[i], cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&s->done[i], cudaEventDisableTiming) != cudaSuccess) {
             const int e = cuda_status(cudaGetLastError());
             gq_session_destroy(s.release());
             return e;
@@ -407,12 +561,15 @@ int gq_session_create(int32_t device, size_t staging_bytes, gq_session_t** out) 
 int gq_session_destroy(gq_session_t* s) {
     if (s == nullptr) return GQ_OK;
     cudaSetDevice(s->device);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kSlots; ++i) {
         if (s->stream[i]) cudaStreamSynchronize(s->stream[i]);
     }
-    for (int i = 0; i < 2; ++i) {
+    s->pool.reset();
+    for (int i = 0; i < kSlots; ++i) {
+        if (s->done[i]) cudaEventDestroy(s->done[i]);
         if (s->stream[i]) cudaStreamDestroy(s->stream[i]);
         if (s->slot[i]) cudaFree(s->slot[i]);
+        if (s->pinned[i]) cudaFreeHost(s->pinned[i]);
     }
     if (s->d_diag) cudaFree(s->d_diag);
     delete s;
@@ -425,15 +582,18 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
     if (count < 0) return GQ_ERR_ARG;
     if (count > 0 && tensors == nullptr) return GQ_ERR_NULL;
     if (!valid_mask(out_mask)) return GQ_ERR_ARG;
+    std::lock_guard<std::mutex> session_lock(s->mu);
     int st = guard_device(s->device);
     if (st != GQ_OK) return st;
 
     std::vector<TypeInfo> info(count);
     std::vector<int64_t> units(count);
+    std::vector<uint8_t> bounce_in(count, 0), bounce_out(count, 0);
+    bool any_bounce = false;
     for (int i = 0; i < count; ++i) {
         int64_t nv = 0;
         // host pointers: alignment of the host copy source does not matter
-        gq_tensor_t t = tensors[i];
+        const gq_tensor_t& t = tensors[i];
         st = shape_check(t, &info[i], &nv, &units[i]);
         if (st != GQ_OK) return st;
         if (nv == 0) continue;
@@ -448,7 +608,28 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
         if (t.perm_heads > 0 &&
             round_up(units[i] * unit_footprint(info[i], out_mask)) + 4 * kAlign > s->slot_bytes)
             return GQ_ERR_SIZE;
+        bounce_in[i] = pageable(t.src);
+        if (info[i].block_values == 0) {
+            bounce_out[i] = pageable(t.values);
+        } else {
+            bounce_out[i] = ((out_mask & GQ_OUT_CODES) && (pageable(t.codes) || pageable(t.scales))) ||
+                            ((out_mask & GQ_OUT_F32) && pageable(t.values));
+        }
+        any_bounce |= bounce_in[i] || bounce_out[i];
     }
+    if (any_bounce && !ensure_bounce(s)) {
+        std::fill(bounce_in.begin(), bounce_in.end(), 0);
+        std::fill(bounce_out.begin(), bounce_out.end(), 0);
+    }
+
+    // on an error after work was queued, let the queued work finish before returning, so
+    // that nothing still writes into the slots or the caller's buffers
+    auto fail = [&](int e) {
+        for (int k = 0; k < kSlots; ++k) cudaStreamSynchronize(s->stream[k]);
+        cudaGetLastError();
+        return e;
+    };
+
     if (host_diags != nullptr && count > s->diag_cap) {
         if (s->d_diag) cudaFree(s->d_diag);
         s->d_diag = nullptr;
@@ -462,16 +643,14 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
     if (host_diags != nullptr && count > 0) {
         st = cuda_status(cudaMemsetAsync(s->d_diag, 0, sizeof(gq_diag_t) * count, s->stream[0]));
         if (st != GQ_OK) return st;
-        // the second stream must not run its kernels before the zeroing
-        cudaEvent_t ev;
-        if ((st = cuda_status(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming))) != GQ_OK) return st;
-        cudaEventRecord(ev, s->stream[0]);
-        cudaStreamWaitEvent(s->stream[1], ev, 0);
-        cudaEventDestroy(ev);
+        // the other streams must not run their kernels before the zeroing
+        if ((st = cuda_status(cudaEventRecord(s->done[0], s->stream[0]))) != GQ_OK) return fail(st);
+        for (int k = 1; k < kSlots; ++k) cudaStreamWaitEvent(s->stream[k], s->done[0], 0);
     }
 
-    // Cut the work into pieces that fill a slot: large tensors are split on unit
-    // boundaries, small ones are packed together.
+    // Cut the work into pieces of about kPieceTarget bytes of slot footprint: large
+    // tensors are split on unit boundaries, small ones are packed together.
+    const size_t target = std::min(s->slot_bytes, kPieceTarget);
     std::vector<std::vector<Member>> pieces;
     {
         std::vector<Member> cur;
@@ -479,16 +658,22 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
         for (int i = 0; i < count; ++i) {
             int64_t done = 0;
             const size_t fp = unit_footprint(info[i], out_mask);
+            const size_t limit = tensors[i].perm_heads > 0 ? s->slot_bytes : target;
             while (done < units[i]) {
-                const size_t room = s->slot_bytes > used + 4 * kAlign ? s->slot_bytes - used - 4 * kAlign : 0;
+                const size_t room = limit > used + 4 * kAlign ? limit - used - 4 * kAlign : 0;
                 int64_t take = static_cast<int64_t>(room / fp);
                 if (tensors[i].perm_heads > 0 && take < units[i]) take = 0;
                 if (take <= 0) {
-                    if (cur.empty()) return GQ_ERR_SIZE;
-                    pieces.push_back(std::move(cur));
-                    cur.clear();
-                    used = 0;
-                    continue;
+                    if (cur.empty()) {
+                        if (limit == s->slot_bytes) return fail(GQ_ERR_SIZE);
+                        take = 1;   // one unit larger than the piece target still fits a slot
+                        if (round_up(fp) + 4 * kAlign > s->slot_bytes) return fail(GQ_ERR_SIZE);
+                    } else {
+                        pieces.push_back(std::move(cur));
+                        cur.clear();
+                        used = 0;
+                        continue;
+                    }
                 }
                 take = std::min<int64_t>(take, units[i] - done);
                 cur.push_back({i, done, take});
@@ -499,24 +684,58 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
         if (!cur.empty()) pieces.push_back(std::move(cur));
     }
 
+    struct Copy {
+        void* dst;
+        const void* src;
+        size_t bytes;
+    };
     std::vector<std::pair<gq::GqDesc, int>> items;
+    std::vector<CopyJob> fill;
+    std::vector<Copy> h2d, d2h;
+    std::vector<CopyJob> drain[kSlots];
+    auto drain_piece = [&](size_t p) -> int {
+        std::vector<CopyJob>& jobs = drain[p % kSlots];
+        if (jobs.empty()) return GQ_OK;
+        const int e = cuda_status(cudaEventSynchronize(s->done[p % kSlots]));
+        if (e != GQ_OK) return e;
+        s->pool->run(jobs);
+        jobs.clear();
+        return GQ_OK;
+    };
     for (size_t p = 0; p < pieces.size(); ++p) {
-        const int k = static_cast<int>(p & 1);
+        const int k = static_cast<int>(p % kSlots);
         cudaStream_t stream = s->stream[k];
         uint8_t* base = s->slot[k];
+        uint8_t* pin = s->pinned[k];
         size_t off = 0;
         items.clear();
-        struct Out { void* host; const void* dev; size_t bytes; };
-        std::vector<Out> outs;
+        fill.clear();
+        h2d.clear();
+        d2h.clear();
+        // an output region at slot offset `o`: straight to the caller's pinned buffer, or
+        // through the pinned slot and a host copy afterwards
+        auto out_region = [&](bool bounce, void* host, size_t o, size_t bytes) {
+            if (bounce) {
+                d2h.push_back({pin + o, base + o, bytes});
+                drain[k].push_back({host, pin + o, bytes});
+            } else {
+                d2h.push_back({host, base + o, bytes});
+            }
+        };
         for (const Member& m : pieces[p]) {
             const gq_tensor_t& t = tensors[m.tensor];
             const TypeInfo& ti = info[m.tensor];
             const size_t src_bytes = static_cast<size_t>(m.units) * ti.unit_bytes;
+            const uint8_t* hsrc = static_cast<const uint8_t*>(t.src) + m.unit0 * ti.unit_bytes;
             uint8_t* dsrc = base + off;
+            if (bounce_in[m.tensor]) {
+                fill.push_back({pin + off, hsrc, src_bytes});
+                h2d.push_back({dsrc, pin + off, src_bytes});
+            } else {
+                h2d.push_back({dsrc, hsrc, src_bytes});
+            }
             off = round_up(off + src_bytes);
-            st = cuda_status(cudaMemcpyAsync(dsrc, static_cast<const uint8_t*>(t.src) + m.unit0 * ti.unit_bytes,
-                                             src_bytes, cudaMemcpyHostToDevice, stream));
-            if (st != GQ_OK) return st;
+            const bool bo = bounce_out[m.tensor];
             gq_tensor_t dt = t;
             dt.rows = t.perm_heads > 0 ? t.rows : m.units * ti.unit_values / t.cols;
             dt.src = dsrc;
@@ -526,25 +745,24 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
             if (ti.block_values == 0) {
                 const size_t vb = static_cast<size_t>(nvals) * ti.unit_bytes;
                 dt.values = reinterpret_cast<float*>(base + off);
+                out_region(bo, static_cast<uint8_t*>(static_cast<void*>(t.values)) + m.unit0 * ti.unit_bytes, off, vb);
                 off = round_up(off + vb);
-                outs.push_back({static_cast<uint8_t*>(static_cast<void*>(t.values)) + m.unit0 * ti.unit_bytes,
-                                dt.values, vb});
             } else {
                 if (out_mask & GQ_OUT_CODES) {
                     dt.codes = base + off;
+                    out_region(bo, static_cast<uint8_t*>(t.codes) + m.unit0 * ti.unit_values, off,
+                               static_cast<size_t>(nvals));
                     off = round_up(off + nvals);
                     dt.scales = reinterpret_cast<float*>(base + off);
                     const int64_t nsc = nvals / ti.block_values;
+                    out_region(bo, t.scales + m.unit0 * (ti.unit_values / ti.block_values), off,
+                               static_cast<size_t>(4 * nsc));
                     off = round_up(off + 4 * nsc);
-                    outs.push_back({static_cast<uint8_t*>(t.codes) + m.unit0 * ti.unit_values, dt.codes,
-                                    static_cast<size_t>(nvals)});
-                    outs.push_back({t.scales + m.unit0 * (ti.unit_values / ti.block_values), dt.scales,
-                                    static_cast<size_t>(4 * nsc)});
                 }
                 if (out_mask & GQ_OUT_F32) {
                     dt.values = reinterpret_cast<float*>(base + off);
+                    out_region(bo, t.values + m.unit0 * ti.unit_values, off, static_cast<size_t>(4 * nvals));
                     off = round_up(off + 4 * static_cast<size_t>(nvals));
-                    outs.push_back({t.values + m.unit0 * ti.unit_values, dt.values, static_cast<size_t>(4 * nvals)});
                 }
             }
             // rows of a piece: whole rows are not required (rows only matter for the
@@ -555,26 +773,34 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
             }
             items.emplace_back(make_desc(dt, ti, m.units), t.type);
         }
-        st = launch_grouped(items, out_mask, stream);
-        if (st != GQ_OK) return st;
-        for (const Out& o : outs) {
-            st = cuda_status(cudaMemcpyAsync(o.host, o.dev, o.bytes, cudaMemcpyDeviceToHost, stream));
-            if (st != GQ_OK) return st;
+        // host side of the input first (once the slot's previous piece, which may still be
+        // reading the pinned slot, has finished), then the piece's GPU work on its stream
+        if (!fill.empty()) {
+            if (p >= kSlots && (st = cuda_status(cudaEventSynchronize(s->done[k]))) != GQ_OK) return fail(st);
+            s->pool->run(fill);
         }
+        for (const Copy& c : h2d) {
+            st = cuda_status(cudaMemcpyAsync(c.dst, c.src, c.bytes, cudaMemcpyHostToDevice, stream));
+            if (st != GQ_OK) return fail(st);
+        }
+        st = launch_grouped(items, out_mask, stream);
+        if (st != GQ_OK) return fail(st);
+        for (const Copy& c : d2h) {
+            st = cuda_status(cudaMemcpyAsync(c.dst, c.src, c.bytes, cudaMemcpyDeviceToHost, stream));
+            if (st != GQ_OK) return fail(st);
+        }
+        if ((st = cuda_status(cudaEventRecord(s->done[k], stream))) != GQ_OK) return fail(st);
+        // while this piece runs, hand the previous piece's results to the caller
+        if (p >= 1 && (st = drain_piece(p - 1)) != GQ_OK) return fail(st);
+    }
+    if (!pieces.empty() && (st = drain_piece(pieces.size() - 1)) != GQ_OK) return fail(st);
+    for (int k = 0; k < kSlots; ++k) {
+        st = cuda_status(cudaStreamSynchronize(s->stream[k]));
+        if (st != GQ_OK) return fail(st);
     }
     if (host_diags != nullptr && count > 0) {
-        // both streams' kernels must finish before the maxima are read
-        cudaEvent_t ev;
-        if ((st = cuda_status(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming))) != GQ_OK) return st;
-        cudaEventRecord(ev, s->stream[1]);
-        cudaStreamWaitEvent(s->stream[0], ev, 0);
-        cudaEventDestroy(ev);
-        st = cuda_status(cudaMemcpyAsync(host_diags, s->d_diag, sizeof(gq_diag_t) * count,
-                                         cudaMemcpyDeviceToHost, s->stream[0]));
-        if (st != GQ_OK) return st;
-    }
-    for (int i = 0; i < 2; ++i) {
-        st = cuda_status(cudaStreamSynchronize(s->stream[i]));
+        // every stream's kernels have finished: read the maxima
+        st = cuda_status(cudaMemcpy(host_diags, s->d_diag, sizeof(gq_diag_t) * count, cudaMemcpyDeviceToHost));
         if (st != GQ_OK) return st;
     }
     return GQ_OK;

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import ctypes
 import logging
+import mmap
 import os
 import threading
 from pathlib import Path
@@ -75,6 +76,27 @@ def _host_ptr(a: np.ndarray) -> int:
     return a.ctypes.data
 
 
+_HUGE_MIN = 8 << 20
+
+
+def _host_empty(shape, dtype) -> np.ndarray:
+    """An uninitialised host array for a conversion result.  Large ones are backed by an
+    anonymous mapping with transparent huge pages requested, so that the first writes
+    (by the library's copy threads) fault in 2 MiB pages instead of 4 KiB ones; the
+    array owns the mapping and frees it with itself."""
+    dtype = np.dtype(dtype)
+    n = int(np.prod(shape)) * dtype.itemsize
+    if n < _HUGE_MIN:
+        return np.empty(shape, dtype=dtype)
+    m = mmap.mmap(-1, n, flags=mmap.MAP_PRIVATE | mmap.MAP_ANONYMOUS)
+    if hasattr(m, "madvise") and hasattr(mmap, "MADV_HUGEPAGE"):
+        try:
+            m.madvise(mmap.MADV_HUGEPAGE)
+        except OSError:
+            pass
+    return np.frombuffer(m, dtype=dtype, count=n // dtype.itemsize).reshape(shape)
+
+
 def convert_host(fmt: str, raw: np.ndarray, rows: int, cols: int, force_float: bool = False,
                  perm_heads: int = 0, device: int | None = None):
     """GGUF bytes in host memory -> (scales | None, weights) in host memory, on the GPU.
@@ -94,12 +116,12 @@ def convert_host(fmt: str, raw: np.ndarray, rows: int, cols: int, force_float: b
     rec.src_bytes = raw.size
     scales = codes = values = None
     if force_float:
-        values = np.empty((rows, cols), dtype=np.float32)
+        values = _host_empty((rows, cols), np.float32)
         rec.values = _host_ptr(values)
         mask = N.OUT_F32
     else:
-        codes = np.empty((rows, cols), dtype=np.int8)
-        scales = np.empty((n_values // f.block_values, 1), dtype=np.float32)
+        codes = _host_empty((rows, cols), np.int8)
+        scales = _host_empty((n_values // f.block_values, 1), np.float32)
         rec.codes = _host_ptr(codes)
         rec.scales = _host_ptr(scales)
         mask = N.OUT_CODES
