@@ -47,6 +47,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-modalix", action="store_true",
+                    help="skip the conversion fused with the Modalix layout (gq_convert_modalix)")
     ap.add_argument("--layers", type=int, default=0,
                     help="keep only the first L transformer layers (small cases for profiling)")
     ap.add_argument("--formats", default="", help="comma list of GGML formats to keep (profiling)")
@@ -382,6 +384,75 @@ def run_ours(args, rank, world, local_rank):
         if fmt in batches and out_mask & N.OUT_CODES:
             diag_ok &= bool((batches[fmt].diags[:, 0] != 0).any().item())
 
+    # ---- the conversion fused with the Modalix weight layout (gq_convert_modalix), one
+    # launch per tensor captured in a CUDA graph, against the two passes it replaces (the
+    # conversion above plus gq_modalix_layout on its results)
+    modalix = None
+    if not args.no_modalix and out_mask == N.OUT_CODES:
+        import ctypes
+        mrecs, lrecs, mbytes, malgo = [], [], 0, 0
+        for t in tensors:
+            f = FORMATS[t.fmt]
+            if not f.block_values:
+                continue
+            oc = torch.empty((t.cols, t.rows), dtype=torch.int8, device=dev)
+            os_ = torch.empty((t.cols // f.block_values, t.rows), dtype=torch.float32, device=dev)
+            r = N.Tensor()
+            r.type, r.perm_heads, r.rows, r.cols = f.type_id, t.perm_heads, t.rows, t.cols
+            r.src, r.src_bytes, r.codes, r.scales = t.src.data_ptr(), t.src.numel(), oc.data_ptr(), os_.data_ptr()
+            mrecs.append((r, oc, os_))
+            lrecs.append((t, oc, os_, f.block_values))
+            mbytes += t.src_bytes
+            malgo += piece_cost(t.fmt, t.rows, t.cols, "codes")
+        # launches go to the current stream (the capture stream while a graph is recorded)
+        def mstep():
+            sid = torch.cuda.current_stream().cuda_stream
+            for r, _, _ in mrecs:
+                N.check(N.lib().gq_convert_modalix(ctypes.byref(r), r.rows, sid), "gq_convert_modalix")
+
+        def lstep():
+            sid = torch.cuda.current_stream().cuda_stream
+            for t, oc, os_, blk in lrecs:
+                N.check(N.lib().gq_modalix_layout(t.codes.data_ptr(), t.scales.data_ptr(), t.rows, t.cols, blk, t.rows,
+                                                  oc.data_ptr(), os_.data_ptr(), sid), "gq_modalix_layout")
+
+        def graph_ms(fn, n):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / n
+            del g
+            return ms
+
+        if mrecs:
+            barrier()
+            m_ms = graph_ms(mstep, 20)
+            l_ms = graph_ms(lstep, 20)
+            agg = torch.tensor([m_ms, l_ms], dtype=torch.float64, device=dev)
+            tot = torch.tensor([float(mbytes), float(malgo)], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(agg, op=dist.ReduceOp.MAX)
+                dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+            m_ms, l_ms = float(agg[0].item()), float(agg[1].item())
+            peak_, _ = measured_peak()
+            modalix = {"value": round(float(tot[0].item()) / (m_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                       "ms_per_model": round(m_ms, 4),
+                       "hbm_frac": round(float(tot[1].item()) / (m_ms / 1e3) / 1e9 / (peak_ * world), 4),
+                       "two_pass_ms_per_model": round(ms_step + l_ms, 4), "layout_pass_ms": round(l_ms, 4),
+                       "launches_per_step": len(mrecs), "api": "gq_convert_modalix (CUDA graph of per-tensor launches)"}
+        del mrecs, lrecs
+
     # ---- end to end through the C ABI host-buffer call (pinned host memory)
     e2e = None
     if not args.no_e2e and args.e2e_steps > 0:
@@ -431,15 +502,39 @@ def run_ours(args, rank, world, local_rank):
                 same &= bool(torch.equal(ht.to(dev, non_blocking=False).view(torch.uint8),
                                          getattr(t, name).view(torch.uint8)))
         N.lib().gq_session_destroy(sess)
+
+        # The drop-in call the reference's GgufModel.load_weight makes, one tensor at a
+        # time: pageable numpy input (as a memory-mapped GGUF file gives it) and freshly
+        # allocated numpy results, through gguf_conversion.convert_host.  Float tensors
+        # are passed through on the host by that API and are left out here.
+        from llima_b200.gguf_conversion import convert_host as dropin
+        quant = [(t, hs.numpy().copy()) for t, hs in zip(tensors, host_src) if FORMATS[t.fmt].block_values]
+        if quant:
+            t0_, r0_ = quant[0]
+            dropin(t0_.fmt, r0_, t0_.rows, t0_.cols, False, t0_.perm_heads)   # session set-up
+        barrier()
+        t0 = time.perf_counter()
+        for t, raw in quant:
+            dropin(t.fmt, raw, t.rows, t.cols, False, t.perm_heads)
+        dropin_s = time.perf_counter() - t0
+        barrier()
+        dropin_bytes = float(sum(r.size for _, r in quant))
+        del quant
         h2d = sum(h.numel() for h in host_src)
         d2h = sum(ht.numel() * ht.element_size() for outs in host_out for ht in outs.values())
-        agg = torch.tensor([float(gguf_bytes), float(h2d), float(d2h), 1.0 if same else 0.0], dtype=torch.float64,
-                           device=dev)
+        agg = torch.tensor([float(gguf_bytes), float(h2d), float(d2h), 1.0 if same else 0.0, dropin_bytes],
+                           dtype=torch.float64, device=dev)
+        tmax = torch.tensor([dropin_s], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(agg, op=dist.ReduceOp.SUM)
+            dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
         e2e = {"value": float(agg[0].item()) / e2e_s / 1e9, "unit": "GB/s", "s_per_model": e2e_s,
                "h2d_bytes_per_step": int(agg[1].item()), "d2h_bytes_per_step": int(agg[2].item()),
-               "matches_device": bool(agg[3].item() == world), "api": "gq_convert_host (pinned host buffers)"}
+               "matches_device": bool(agg[3].item() == world), "api": "gq_convert_host (pinned host buffers)",
+               "dropin_pageable": {"value": round(float(agg[4].item()) / float(tmax.item()) / 1e9, 3), "unit": "GB/s",
+                                   "s_per_model": round(float(tmax.item()), 4),
+                                   "api": "gguf_conversion.convert_host, one call per tensor, pageable numpy "
+                                          "in/out (GgufModel.load_weight's path)"}}
         del host_src, host_out
 
     tot = torch.tensor([float(gguf_bytes), float(out_bytes), 1.0 if diag_ok else 0.0], dtype=torch.float64,
@@ -469,7 +564,7 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded, BASELINE distributions)",
         "config": workload_config(args, world),
         "roofline": roofline, "gpu_launches": launches_per_step * args.steps, "diag_written": bool(tot[2].item() == world),
-        "e2e": e2e, "clocks": clocks,
+        "e2e": e2e, "clocks": clocks, "modalix_fused": modalix,
     }
     return line
 

@@ -26,6 +26,8 @@
  *   gq_requantize_symmetric         sima_lmm/gguf/ggml_quant.py:785-886 (requantize_symmetric)
  *   gq_query                        sizes implied by ggml_quant.py:104-131 (format table)
  *   gq_convert_host                 the same as gq_convert_batch, on host buffers
+ *   gq_convert_modalix              unpack_gguf_tensor followed by ModelGraph._build_conv's
+ *                                   layout (sima_lmm/model/model_graph.py:1012-1079), fused
  *   gq_unpack_fields                sima_lmm/gguf/ggml_quant.py:567-694 (unpack_k_quant) and
  *                                   :174-271 (unpack_q4 / unpack_q5, ASYMMETRIC)
  *   gq_remove_superblocks           sima_lmm/gguf/ggml_quant.py:739-782 (remove_superblocks)
@@ -156,6 +158,19 @@ GQ_API int gq_requantize_symmetric(const float* block_consts, const int8_t* code
 GQ_API int gq_modalix_layout(const void* codes, const float* scales, int64_t rows, int64_t cols,
                              int32_t block_values, int64_t rows_padded, void* out_codes, float* out_scales,
                              void* stream);
+
+/* The conversion and the Modalix layout in one pass: unpack_gguf_tensor (+ the llama q/k
+ * head permutation when perm_heads > 0; gguf_conversion.py:102-176, 314-332) followed by
+ * ModelGraph._build_conv's reshape / transposes (model_graph.py:1012-1079), without the
+ * row-major codes ever reaching memory.  tensor->codes receives (cols, rows_padded) bytes
+ * (the memory order of the HWIGO weight (1, 1, cols, 1, rows_padded)), tensor->scales
+ * (cols / block, rows_padded) f32; output channels rows..rows_padded-1 are the int4
+ * 32-way padding: zero codes, unit scales.  tensor->values is not used; tensor->diag, if
+ * any, is zeroed and receives the requantization maxima.  Takes cols a multiple of 256
+ * and row lengths of a whole number of 16-byte chunks (cols / 256 * 210 for Q6_K, etc.);
+ * other shapes return GQ_ERR_SIZE (convert, then gq_modalix_layout).  Device pointers:
+ * src 16-byte aligned, scales 4. */
+GQ_API int gq_convert_modalix(const gq_tensor_t* tensor, int64_t rows_padded, void* stream);
 
 /* The field-level steps of the reference's ggml_quant module, for callers that use them
  * one by one (the conversion entry points above fuse them).

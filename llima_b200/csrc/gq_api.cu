@@ -249,6 +249,47 @@ int gq_requantize_symmetric(const float* block_consts, const int8_t* codes, int6
                                           out_codes, diag, stream));
 }
 
+int gq_convert_modalix(const gq_tensor_t* tensor, int64_t rows_padded, void* stream) {
+    if (tensor == nullptr) return GQ_ERR_NULL;
+    const gq_tensor_t& t = *tensor;
+    TypeInfo ti;
+    int64_t nv = 0, nu = 0;
+    const int st = shape_check(t, &ti, &nv, &nu);
+    if (st != GQ_OK) return st;
+    if (ti.block_values == 0) return GQ_ERR_TYPE;
+    if (rows_padded < t.rows || rows_padded > INT32_MAX) return GQ_ERR_SIZE;
+    // whole 256-channel column tiles, and every row's bytes starting on a 16-byte boundary
+    if (t.cols % gq::kModalixCols != 0) return GQ_ERR_SIZE;
+    const int64_t upr = t.cols / ti.unit_values;
+    if ((upr * ti.unit_bytes) % 16 != 0) return GQ_ERR_SIZE;
+    if (t.cols == 0 || rows_padded == 0) return GQ_OK;
+    if (t.codes == nullptr || t.scales == nullptr) return GQ_ERR_NULL;
+    if (t.rows > 0 && t.src == nullptr) return GQ_ERR_NULL;
+    if (!aligned(t.src, 16) || !aligned(t.scales, 4)) return GQ_ERR_ALIGN;
+    if (t.diag != nullptr) {
+        if (!aligned(t.diag, 4)) return GQ_ERR_ALIGN;
+        const int e = gq_diag_reset(t.diag, 1, stream);
+        if (e != GQ_OK) return e;
+    }
+    gq::GqModalix m{};
+    m.src = static_cast<const uint8_t*>(t.src);
+    m.out_codes = static_cast<uint8_t*>(t.codes);
+    m.out_scales = t.scales;
+    m.diag = (ti.asym && t.diag != nullptr) ? t.diag : nullptr;
+    m.rows = t.rows;
+    m.cols = t.cols;
+    m.rows_padded = rows_padded;
+    m.units_per_row = upr;
+    const int64_t n_col = t.cols / gq::kModalixCols;
+    const int64_t n_tiles = (rows_padded + gq::kModalixRows - 1) / gq::kModalixRows * n_col;
+    if (n_tiles >= (int64_t(1) << 31)) return GQ_ERR_SIZE;
+    m.n_col_tiles = static_cast<uint32_t>(n_col);
+    m.n_tiles = static_cast<uint32_t>(n_tiles);
+    gq::fast_div_params(m.n_col_tiles, m.ncol_mul, m.ncol_shift);
+    m.head_dim = t.perm_heads > 0 ? static_cast<int32_t>(t.rows / t.perm_heads) : 0;
+    return cuda_status(gq::launch_modalix(t.type, m, stream));
+}
+
 int gq_unpack_fields(int32_t type, const void* src, size_t src_bytes, int64_t n_units, float* super_consts,
                      int8_t* block_consts, int8_t* values, void* stream) {
     TypeInfo ti;

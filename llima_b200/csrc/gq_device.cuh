@@ -54,6 +54,10 @@ __device__ __forceinline__ void stg128f(float* p, float a, float b, float c, flo
     st_global(reinterpret_cast<float4*>(p), make_float4(a, b, c, d));
 }
 
+// Code / scale store of a conversion (defined with the shared-memory helpers below).
+template <int MODE, class T>
+__device__ __forceinline__ void st_out(T* p, T v);
+
 // ---- per-block requantization parameters (requantize_symmetric) --------------------
 
 #ifndef GQ_RQ_BRANCHLESS
@@ -229,6 +233,7 @@ __device__ __forceinline__ FastRequant requant_fast(float S, float M, int qmin, 
 // sf0 (ggml_quant.py:859-882): sf, rm and the block scale as requant_block derives them,
 // the per-value codes and the clipping error as the largest |clip(v) - v| of the block.
 // Returns the block's rounding and clipping errors (the same in every lane).
+template <int MODE = kOutCodes>
 __device__ __forceinline__ gq_diag_t finish_block(int q, float S, float r, float sf0, int lo_out, int hi_out,
                                                   uint8_t* code, float* scale, int lane) {
     const bool big = sf0 > 0.98f;
@@ -238,8 +243,8 @@ __device__ __forceinline__ gq_diag_t finish_block(int q, float S, float r, float
     const int c = f32_to_i16_x86(rintf(__fmul_rn(static_cast<float>(q), sf)));
     const int u = static_cast<int>(static_cast<short>(c + rm));
     const int v = min(max(u, lo_out), hi_out);
-    st_global(code, static_cast<uint8_t>(v));
-    if (lane == 0) st_global(scale, __fdiv_rn(S, sf));
+    st_out<MODE>(code, static_cast<uint8_t>(v));
+    if (lane == 0) st_out<MODE>(scale, __fdiv_rn(S, sf));
     gq_diag_t e;
     e.round_err_bits = __float_as_uint(fabsf(__fsub_rn(rintf(rmv), rmv)));
     e.clip_err = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(abs(v - u))));
@@ -353,6 +358,54 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src,
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
+
+// ---- code / scale stores of a conversion ---------------------------------------------
+
+// Shared row tiles of 256-byte rows (the fused Modalix writer) keep their 16-byte chunks
+// XOR-swizzled by row: chunk c of the row at shared-address bits 8..11 = r sits at chunk
+// c ^ r, so that the decode's stores (lanes 64 or 16 bytes apart over 8 rows) and the
+// transpose's column reads spread over all banks.  A bijection on every 256-byte block.
+__device__ __forceinline__ uint32_t row_swizzle(uint32_t a) { return a ^ (((a >> 8) & 15u) << 4); }
+
+__device__ __forceinline__ void sts(uint32_t a, uint8_t v) {
+    asm volatile("st.shared.u8 [%0], %1;" ::"r"(a), "r"(static_cast<uint32_t>(v)) : "memory");
+}
+__device__ __forceinline__ void sts(uint32_t a, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void sts(uint32_t a, float2 v) {
+    asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(v.x), "f"(v.y) : "memory");
+}
+__device__ __forceinline__ void sts(uint32_t a, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void sts(uint32_t a, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
+
+// Code / scale stores: to global memory, or (kOutSmem) to a shared tile (codes swizzled
+// as above, scales as they are).
+template <int MODE, class T>
+__device__ __forceinline__ void st_out(T* p, T v) {
+    if constexpr ((MODE & kOutSmem) != 0) {
+        const uint32_t a = smem_u32addr(p);
+        if constexpr (sizeof(T) == 1 || sizeof(T) == 16) {
+            sts(row_swizzle(a), v);
+        } else {
+            sts(a, v);
+        }
+    } else {
+        st_global(p, v);
+    }
+}
+template <int MODE>
+__device__ __forceinline__ void st_out128(void* p, uint4 v) { st_out<MODE>(reinterpret_cast<uint4*>(p), v); }
 
 // ---- misc ------------------------------------------------------------------------------
 

@@ -47,11 +47,30 @@ struct GqBatch {
     GqDesc d[kMaxDesc];
 };
 
-enum : int { kOutCodes = GQ_OUT_CODES, kOutF32 = GQ_OUT_F32 };
+// kOutSmem (internal): the codes and scales go to a shared-memory tile instead of the
+// tensor's global buffers (the fused Modalix layout writer transposes them from there)
+enum : int { kOutCodes = GQ_OUT_CODES, kOutF32 = GQ_OUT_F32, kOutSmem = 4 };
+
+// One tensor converted straight into the Modalix weight layout (gq_convert_modalix).
+struct GqModalix {
+    const uint8_t* src;       // GGUF bytes, rows x units_per_row stored units
+    uint8_t* out_codes;       // (cols, rows_padded)
+    float* out_scales;        // (cols / block, rows_padded)
+    gq_diag_t* diag;          // optional requantization diagnostics
+    int64_t rows, cols, rows_padded;
+    int64_t units_per_row;
+    uint32_t n_col_tiles, n_tiles;
+    uint32_t ncol_mul, ncol_shift;   // division by n_col_tiles (fast_div_params)
+    int32_t head_dim;         // > 0: llama q/k head permutation with heads of this size
+    int32_t pad;
+};
 
 // launch entry points implemented in gq_kernels.cu
 int launch_batch(int type, int out_mask, const GqBatch& batch, void* stream);
 int64_t tiles_for(int type, int64_t n_units);
+int launch_modalix(int type, const GqModalix& m, void* stream);
+constexpr int kModalixRows = 128;   // output channels per tile of the fused layout writer
+constexpr int kModalixCols = 256;   // input channels per tile
 int launch_layout(const uint8_t* codes, const float* scales, int64_t rows, int64_t cols, int64_t nb,
                   int64_t rows_padded, uint8_t* out_codes, float* out_scales, void* stream);
 int64_t embed_max_row_bytes();

@@ -239,7 +239,7 @@ __device__ __forceinline__ void k45_block_constants(const uint8_t* sbp, int b, f
 // takes value k: the low (H = false) or high nibble of byte k of the block's group,
 // with Q5_K's fifth bit; min / max come from warp reductions, then requant_block and the
 // per-value formula (ggml_quant.py:785-886).  Returns the block's diagnostics.
-template <bool Q5>
+template <bool Q5, int MODE>
 __device__ __noinline__ gq_diag_t k45_block_exact(const uint8_t* sbp, int g, bool H, int lane, uint8_t* codes,
                                                   float* scale, const float* recip) {
     constexpr int QS = Q5 ? 48 : 16;
@@ -251,8 +251,8 @@ __device__ __noinline__ gq_diag_t k45_block_exact(const uint8_t* sbp, int g, boo
     float S, M;
     k45_block_constants(sbp, 2 * g + (H ? 1 : 0), S, M);
     const Requant p = requant_block(S, M, qmin, qmax, -128, 127, recip);
-    st_global(codes + lane, static_cast<uint8_t>(requant_value(q, p.sf, p.rm, -128, 127)));
-    if (lane == 0) st_global(scale, p.scale);
+    st_out<MODE>(codes + lane, static_cast<uint8_t>(requant_value(q, p.sf, p.rm, -128, 127)));
+    if (lane == 0) st_out<MODE>(scale, p.scale);
     gq_diag_t diag;
     diag.round_err_bits = __float_as_uint(p.round_err);
     diag.clip_err = p.clip_err;
@@ -341,7 +341,7 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
         const FastRequant pL = requant_fast(SL, ML, qminL, qmaxL, -128, 127, recip);
         const FastRequant pH = requant_fast(SH, MH, qminH, qmaxH, -128, 127, recip);
         if (valid) {
-            st_global(reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g), make_float2(pL.scale, pH.scale));
+            st_out<MODE>(reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g), make_float2(pL.scale, pH.scale));
             acc.add(fmaxf(pL.round_err, pH.round_err), 0);
         }
         constexpr uint32_t kBias = 0x400u;   // lane value q*sf + rm + bias stays in [0, 4096)
@@ -361,12 +361,12 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
         }
         uint8_t* base = D.codes + off;
         if (valid && pL.good) {
-            stg128(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
-            stg128(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
+            st_out128<MODE>(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
+            st_out128<MODE>(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
         }
         if (valid && pH.good) {
-            stg128(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
-            stg128(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
+            st_out128<MODE>(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
+            st_out128<MODE>(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
         }
         // the other blocks (about 0.5%): one warp pass each, after the scale stores above;
         // a block with finite constants is finished from its lane's r and sf0, one with a
@@ -393,13 +393,13 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
                 if (!(which & (1 << side))) continue;
                 gq_diag_t e;
                 if (which & (4 << side)) {
-                    e = k45_block_exact<Q5>(ssbp, sg, side == 1, lane, D.codes + soff + 32 * side,
+                    e = k45_block_exact<Q5, MODE>(ssbp, sg, side == 1, lane, D.codes + soff + 32 * side,
                                             D.scales + (soff >> 5) + side, recip);
                 } else {
                     const float bS = __shfl_sync(kFull, side ? SH : SL, src);
                     const float br = __shfl_sync(kFull, side ? pH.r : pL.r, src);
                     const float bsf0 = __shfl_sync(kFull, side ? pH.sf0 : pL.sf0, src);
-                    e = finish_block(side ? qhi : qlo, bS, br, bsf0, -128, 127, D.codes + soff + 32 * side + lane,
+                    e = finish_block<MODE>(side ? qhi : qlo, bS, br, bsf0, -128, 127, D.codes + soff + 32 * side + lane,
                                      D.scales + (soff >> 5) + side, lane);
                 }
                 acc.add(__uint_as_float(e.round_err_bits), e.clip_err);
@@ -436,7 +436,8 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
 // Q6_K: ql[128] | qh[64] | scales int8[16] | d  (ggml_quant.py:662-679) -> 16 blocks of 16
 // ---------------------------------------------------------------------------------------
 
-template <int MODE>
+// STRIDE: bytes from one super-block of the tile to the next (210 when packed)
+template <int MODE, int STRIDE = 210>
 __device__ __forceinline__ void process_q6k(const GqDesc& D, int64_t unit0, int nunits,
                                             const uint8_t* tile, int lane) {
 #pragma unroll
@@ -445,7 +446,7 @@ __device__ __forceinline__ void process_q6k(const GqDesc& D, int64_t unit0, int 
         const int sb = c >> 4;
         if (sb >= nunits) continue;
         const int kb = c & 15;
-        const uint8_t* sbp = tile + sb * 210;
+        const uint8_t* sbp = tile + sb * STRIDE;
         const float d = h2f(lds16(sbp + 208));
         const int sc = static_cast<int>(static_cast<int8_t>(sbp[192 + kb]));
         // value 128*hh + 32*g + j: nibble of ql[64hh + 32(g&1) + j] (low for g<2),
@@ -465,9 +466,9 @@ __device__ __forceinline__ void process_q6k(const GqDesc& D, int64_t unit0, int 
         const int64_t ou = permute_unit(D, unit0 + sb);
         const int64_t off = ou * 256 + 16 * kb;
         if (MODE & kOutCodes) {
-            stg128(D.codes + off, make_uint4(code[0], code[1], code[2], code[3]));
+            st_out128<MODE>(D.codes + off, make_uint4(code[0], code[1], code[2], code[3]));
             // block scale f16(f32(sc) * f32(d)) (ggml_quant.py:771-773), no requant (:700)
-            st_global(D.scales + ou * 16 + kb, round_to_f16(__fmul_rn(static_cast<float>(sc), d)));
+            st_out<MODE>(D.scales + ou * 16 + kb, round_to_f16(__fmul_rn(static_cast<float>(sc), d)));
         }
         if (MODE & kOutF32) {
             // gguf-py Q6_K.dequantize_blocks: (d * sc) * q
@@ -494,7 +495,7 @@ __device__ __forceinline__ void process_q0(const GqDesc& D, int64_t unit0, int n
                                            const uint8_t* tile, int lane) {
     constexpr int UB = Q4 ? 18 : 34;
     if ((MODE & kOutCodes) && lane < nunits) {
-        st_global(D.scales + permute_unit(D, unit0 + lane), h2f(lds16(tile + UB * lane)));
+        st_out<MODE>(D.scales + permute_unit(D, unit0 + lane), h2f(lds16(tile + UB * lane)));
     }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -511,7 +512,7 @@ __device__ __forceinline__ void process_q0(const GqDesc& D, int64_t unit0, int n
             for (int i = 0; i < 4; ++i) x[i] = ((x[i] >> (4 * h)) & 0x0F0F0F0Fu) ^ 0x08080808u;
         }
         const int64_t off = permute_unit(D, unit0 + b) * 32 + 16 * h;
-        if (MODE & kOutCodes) stg128(D.codes + off, make_uint4(x[0], x[1], x[2], x[3]));
+        if (MODE & kOutCodes) st_out128<MODE>(D.codes + off, make_uint4(x[0], x[1], x[2], x[3]));
         if (MODE & kOutF32) {
             const float d = h2f(lds16(bp));
             float* dst = D.values + off;
@@ -607,9 +608,9 @@ __device__ __forceinline__ void process_q32(const GqDesc& D, int64_t unit0, int 
             for (int i = 0; i < 8; ++i) c[i] = (q[i] + 0x70707070u) ^ 0x80808080u;
         }
         if (valid) {
-            st_global(D.scales + ou, scale);
-            stg128(D.codes + ou * 32, make_uint4(c[0], c[1], c[2], c[3]));
-            stg128(D.codes + ou * 32 + 16, make_uint4(c[4], c[5], c[6], c[7]));
+            st_out<MODE>(D.scales + ou, scale);
+            st_out128<MODE>(D.codes + ou * 32, make_uint4(c[0], c[1], c[2], c[3]));
+            st_out128<MODE>(D.codes + ou * 32 + 16, make_uint4(c[4], c[5], c[6], c[7]));
         }
     }
     if ((MODE & kOutF32) && valid) {
@@ -629,7 +630,8 @@ __device__ __forceinline__ void process_q32(const GqDesc& D, int64_t unit0, int 
     }
 }
 
-template <int TYPE, int MODE>
+// STRIDE: bytes from one super-block of the tile to the next (the unit size when packed)
+template <int TYPE, int MODE, int STRIDE = Fmt<TYPE>::kUnitBytes>
 __device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int nunits, const uint8_t* tile,
                                             int lane, DiagAcc& acc, const float* recip) {
     constexpr bool kQ2 = TYPE == GQ_TYPE_Q2_K;
@@ -640,14 +642,14 @@ __device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int 
         const int sb = c >> 4;
         const bool valid = sb < nunits;
         const int kb = c & 15;
-        const uint8_t* sbp = tile + sb * UB;
+        const uint8_t* sbp = tile + sb * STRIDE;
         const int h = kb >> 3, j = (kb >> 1) & 3, b0 = 16 * (kb & 1);
         uint32_t q[4];
         float d, dmin = 0.0f;
         int sc, mn = 0;
         if (kQ2) {
             // scales[16] | qs[64] | d | dmin; value 128h + 32j + b = bits 2j..2j+1 of qs[32h + b]
-            const uint32_t sbyte = tile[sb * UB + kb];
+            const uint32_t sbyte = sbp[kb];
             sc = sbyte & 0xF;
             mn = sbyte >> 4;
             d = h2f(lds16(sbp + 80));
@@ -687,15 +689,15 @@ __device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int 
                 for (int i = 0; i < 4; ++i) cw[i] = requant_word(q[i], p);
                 if (valid) {
                     acc.add(p.round_err, p.clip_err);
-                    st_global(D.scales + ou * 16 + kb, p.scale);
+                    st_out<MODE>(D.scales + ou * 16 + kb, p.scale);
                 }
             } else {
                 // Q3_K: codes q - 4 (per byte, q <= 7: (q + 0x7C) ^ 0x80), scale f16(sc * d)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) cw[i] = (q[i] + 0x7C7C7C7Cu) ^ 0x80808080u;
-                if (valid) st_global(D.scales + ou * 16 + kb, S);
+                if (valid) st_out<MODE>(D.scales + ou * 16 + kb, S);
             }
-            if (valid) stg128(D.codes + ou * 256 + 16 * kb, make_uint4(cw[0], cw[1], cw[2], cw[3]));
+            if (valid) st_out128<MODE>(D.codes + ou * 256 + 16 * kb, make_uint4(cw[0], cw[1], cw[2], cw[3]));
         }
         if ((MODE & kOutF32) && valid) {
             // gguf-py: Q2_K (d*sc)*q - dmin*m; Q3_K (d*sc)*(q - 4)
@@ -875,6 +877,209 @@ __global__ void __launch_bounds__(kThreads) gq_requant_kernel(const float* __res
 }
 
 // ---------------------------------------------------------------------------------------
+// Conversion fused with the Modalix weight layout (ModelGraph._build_conv,
+// sima_lmm/model/model_graph.py:1012-1079): codes (rows, cols) -> (cols, rows_padded) and
+// block scales (rows, cols / B) -> (cols / B, rows_padded), written in one pass.
+//
+// A CTA owns a tile of 128 output channels (rows of the converted tensor in output order;
+// the llama q/k head permutation becomes a gather of source rows) x 256 input channels.
+// Each warp copies the stored bytes of its 16 rows with cp.async: the 16-byte-aligned span
+// around each row's segment, so a unit sits `shift` bytes into its slot (0 unless the
+// unit size is not a multiple of 16).  The format's decode runs unchanged with its code /
+// scale stores directed to a shared row tile (kOutSmem).  The row tile is transposed in
+// 4x4-byte blocks (PRMT) into a column tile whose 4-byte words are XOR-swizzled by row,
+// so that both the transpose and the final read are free of bank conflicts, and written
+// out as 16-byte stores along output channels.  Output channels rows..rows_padded-1 are
+// the layout's padding: zero codes and unit scales.
+// ---------------------------------------------------------------------------------------
+
+template <int TYPE>
+struct MxFmt {
+    static constexpr int UB = Fmt<TYPE>::kUnitBytes;
+    static constexpr bool K = TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K || TYPE == GQ_TYPE_Q6_K ||
+                              TYPE == GQ_TYPE_Q2_K || TYPE == GQ_TYPE_Q3_K;
+    static constexpr int UNITS = K ? 1 : 8;                 // stored units per row of a tile
+    static constexpr int SEG = UNITS * UB;                  // bytes of one row's segment
+    // slot stride: the segment plus room for the alignment shift
+    static constexpr int STR = (SEG % 16 == 0) ? SEG : ((SEG + 15 + 15) / 16) * 16;
+    static constexpr int CH = STR / 16;                     // 16-byte chunks per slot
+    static constexpr int NBS = 256 / (TYPE == GQ_TYPE_Q6_K || TYPE == GQ_TYPE_Q2_K || TYPE == GQ_TYPE_Q3_K ? 16 : 32);
+    static constexpr int kWarpStaging = 16 * STR + 16;      // + slack for lds128_align2
+    static constexpr int kTBytes = kModalixCols * kModalixRows;   // column tile (bytes)
+    static constexpr int kRBytes = kModalixRows * kModalixCols;   // row tile
+    static constexpr int kSBytes = kModalixRows * 16 * 4;         // scale tile (up to 16 per row)
+    static constexpr int kSmem = kTBytes + kRBytes + kSBytes + 8 * kWarpStaging + 1024;   // + alignment
+};
+
+// Source row of output channel o (inverse of the q/k permutation of
+// gguf_conversion.py:314-332: row 2a + t of a head moves to t * D/2 + a).
+__device__ __forceinline__ uint32_t modalix_src_row(const GqModalix& m, uint32_t o) {
+    if (m.head_dim == 0) return o;
+    const uint32_t d = static_cast<uint32_t>(m.head_dim), half = d >> 1;
+    const uint32_t h = o / d, rem = o - h * d;
+    const uint32_t t = rem >= half ? 1u : 0u, a = rem - t * half;
+    return h * d + 2 * a + t;
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constant__ GqModalix m) {
+    using X = MxFmt<TYPE>;
+    constexpr int MODE = kOutCodes | kOutSmem;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    __shared__ float recip[17];
+    if (threadIdx.x < 17) recip[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, static_cast<float>(threadIdx.x)) : 0.0f;
+    // the tiles start on a 1 KiB boundary (the row tile's swizzle works on 256-byte blocks)
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* rtile = smem + X::kTBytes;                                        // 128 rows x 256 bytes
+    float* stile = reinterpret_cast<float*>(smem + X::kTBytes + X::kRBytes);   // 128 rows x NBS
+    const uint32_t t_s = smem_u32addr(smem);                                   // 256 rows x 32 words
+    const uint32_t r_s = smem_u32addr(rtile);
+    const uint32_t s_s = smem_u32addr(stile);
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    uint8_t* staging = smem + X::kTBytes + X::kRBytes + X::kSBytes + warp * X::kWarpStaging;
+    __syncthreads();
+    const uint32_t ncol = m.n_col_tiles, rows = static_cast<uint32_t>(m.rows);
+
+    // tile t: row block rb (output channels d0..d0+127), column block cb (256 input channels)
+    auto issue = [&](uint32_t t) {
+        if (t >= m.n_tiles) return;
+        const uint32_t rb = fast_div(t, m.ncol_mul, m.ncol_shift), cb = t - rb * ncol;
+        const uint32_t o_lane = rb * kModalixRows + 16 * warp + (lane & 15);
+        // lanes 0..15: byte offset of row (lane)'s segment, or -1 past the last row
+        int64_t seg = -1;
+        if (o_lane < rows)
+            seg = (static_cast<int64_t>(modalix_src_row(m, o_lane)) * m.units_per_row + cb * X::UNITS) * X::UB;
+        // every lane runs the same trips (the shuffle needs the whole warp)
+        for (int base = 0; base < 16 * X::CH; base += 32) {
+            const int q = base + lane;
+            const int lr = q < 16 * X::CH ? q / X::CH : 15, c = q - lr * X::CH;
+            const int64_t off = __shfl_sync(0xffffffffu, seg, lr);
+            if (q >= 16 * X::CH || off < 0) continue;
+            const int64_t start = (off & ~int64_t(15)) + 16 * c, end = off + X::SEG;
+            if (start >= end) continue;
+            cp_async16(staging + lr * X::STR + 16 * c, m.src + start, end - start < 16 ? static_cast<int>(end - start) : 16);
+        }
+        cp_async_commit();
+    };
+
+    DiagAcc acc;
+    acc.target = m.diag;
+    GqDesc dt{};
+    dt.codes = rtile;
+    dt.scales = stile;
+    dt.diag = m.diag;
+
+    uint32_t t = blockIdx.x;
+    issue(t);
+    for (; t < m.n_tiles; t += gridDim.x) {
+        const uint32_t rb = fast_div(t, m.ncol_mul, m.ncol_shift), cb = t - rb * ncol;
+        const uint32_t d0 = rb * kModalixRows;
+        // rows of this tile below `rows` (0..128)
+        const int valid_rows = d0 >= rows ? 0 : (rows - d0 < kModalixRows ? static_cast<int>(rows - d0) : kModalixRows);
+        const int shift = static_cast<int>((cb * X::SEG) & 15);   // row starts are 16-byte aligned
+        cp_async_wait<0>();
+        __syncwarp();
+        // phase A: decode this warp's 16 rows into the row tile / scale tile
+        if constexpr (X::K) {
+#pragma unroll 1
+            for (int sub = 0; sub < 2; ++sub) {
+                const int left = valid_rows - (16 * warp + 8 * sub);
+                const int n = left <= 0 ? 0 : (left < 8 ? left : 8);
+                if (n == 0) continue;
+                const uint8_t* tile = staging + 8 * sub * X::STR + shift;
+                const int u0 = 16 * warp + 8 * sub;
+                if constexpr (TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K) {
+                    process_k45<TYPE == GQ_TYPE_Q5_K, MODE>(dt, u0, n, tile, lane, acc, recip);
+                } else if constexpr (TYPE == GQ_TYPE_Q6_K) {
+                    process_q6k<MODE, X::STR>(dt, u0, n, tile, lane);
+                } else {
+                    process_k16<TYPE, MODE, X::STR>(dt, u0, n, tile, lane, acc, recip);
+                }
+            }
+        } else {
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j) {
+                const int left = valid_rows - (16 * warp + 4 * j);
+                const int n = left <= 0 ? 0 : (left < 4 ? left * 8 : 32);
+                if (n == 0) continue;
+                const uint8_t* tile = staging + 4 * j * X::STR;
+                const int u0 = (16 * warp + 4 * j) * 8;
+                if constexpr (TYPE == GQ_TYPE_Q8_0 || TYPE == GQ_TYPE_Q4_0) {
+                    process_q0<TYPE == GQ_TYPE_Q4_0, MODE>(dt, u0, n, tile, lane);
+                } else {
+                    process_q32<TYPE, MODE>(dt, u0, n, tile, lane, acc, recip);
+                }
+            }
+        }
+        __syncthreads();
+        // phase B: the next tile's copies go out; transpose codes into the column tile
+        // (word a of column-tile row 4b + k at a ^ (b & 31)); scales straight out
+        issue(t + gridDim.x);
+#pragma unroll 2
+        for (int it = 0; it < 8; ++it) {
+            const int a = warp + 8 * (it >> 1);       // output channels 4a..4a+3
+            const int b = lane + 32 * (it & 1);       // input channels 4b..4b+3
+            uint32_t x[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                x[j] = (4 * a + j < valid_rows) ? lds_u32(row_swizzle(r_s + (4 * a + j) * 256 + 4 * b)) : 0u;
+            const uint32_t t0 = __byte_perm(x[0], x[1], 0x5140), t1 = __byte_perm(x[0], x[1], 0x7362);
+            const uint32_t t2 = __byte_perm(x[2], x[3], 0x5140), t3 = __byte_perm(x[2], x[3], 0x7362);
+            const uint32_t tw = t_s + 4 * (b * 128 + (a ^ (b & 31)));
+            sts(tw, __byte_perm(t0, t2, 0x5410));
+            sts(tw + 128, __byte_perm(t0, t2, 0x7632));
+            sts(tw + 256, __byte_perm(t1, t3, 0x5410));
+            sts(tw + 384, __byte_perm(t1, t3, 0x7632));
+        }
+        const int64_t rp = m.rows_padded;
+        for (int task = threadIdx.x; task < X::NBS * 32; task += 256) {
+            const int bb = task % X::NBS, quad = task / X::NBS;   // scale column, 4 output channels
+            const int64_t o0 = d0 + 4 * quad;
+            if (o0 >= rp) continue;
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                v[e] = (4 * quad + e < valid_rows) ? __uint_as_float(lds_u32(s_s + 4 * ((4 * quad + e) * X::NBS + bb))) : 1.0f;
+            float* dst = m.out_scales + static_cast<int64_t>(cb * X::NBS + bb) * rp + o0;
+            if (o0 + 4 <= rp && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                st_global(reinterpret_cast<float4*>(dst), make_float4(v[0], v[1], v[2], v[3]));
+            } else {
+                for (int e = 0; e < 4 && o0 + e < rp; ++e) st_global(dst + e, v[e]);
+            }
+        }
+        __syncthreads();
+        // phase C: column tile -> codes, 16 output channels per lane
+        const int q = lane & 7;                                               // output channels 16q..16q+15
+        const int64_t o0 = d0 + 16 * q;
+        const bool full = o0 + 16 <= rp;
+#pragma unroll 2
+        for (int it = 0; it < 8; ++it) {
+            const int idx = warp * 8 + it;
+            const int i = 16 * (idx >> 2) + (idx & 3) + 4 * (lane >> 3);   // input channel in the tile
+            if (o0 >= rp) continue;
+            const uint32_t rowa = t_s + 128 * i;
+            const int sw = (i >> 2) & 31;
+            uint4 w;
+            w.x = lds_u32(rowa + 4 * ((4 * q + 0) ^ sw));
+            w.y = lds_u32(rowa + 4 * ((4 * q + 1) ^ sw));
+            w.z = lds_u32(rowa + 4 * ((4 * q + 2) ^ sw));
+            w.w = lds_u32(rowa + 4 * ((4 * q + 3) ^ sw));
+            uint8_t* dst = m.out_codes + static_cast<int64_t>(cb * kModalixCols + i) * rp + o0;
+            if (full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                stg128(dst, w);
+            } else {
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+                for (int e = 0; e < 16 && o0 + e < rp; ++e)
+                    st_global(dst + e, static_cast<uint8_t>(ws[e >> 2] >> (8 * (e & 3))));
+            }
+        }
+    }
+    cp_async_wait<0>();
+    acc.flush(lane);
+}
+
+// ---------------------------------------------------------------------------------------
 // Host-side launchers
 // ---------------------------------------------------------------------------------------
 
@@ -955,6 +1160,48 @@ int64_t tiles_for(int type, int64_t n_units) {
         default: upt = kCopyTileBytes / 2; break;   // F16, BF16
     }
     return (n_units + upt - 1) / upt;
+}
+
+namespace {
+
+template <int TYPE>
+int launch_modalix_t(const GqModalix& m, cudaStream_t s) {
+    using X = MxFmt<TYPE>;
+    static_assert(X::kSmem <= 113 * 1024, "two CTAs per SM");
+    static int per_sm[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int& occ = per_sm[dev & 63];
+    if (occ == 0) {
+        cudaFuncSetAttribute(gq_modalix_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, X::kSmem);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gq_modalix_kernel<TYPE>, 256, X::kSmem) != cudaSuccess ||
+            occ < 1)
+            occ = 1;
+    }
+    const int64_t cap = static_cast<int64_t>(device_info().sms) * occ;
+    const int blocks = static_cast<int>(m.n_tiles < cap ? m.n_tiles : cap);
+    if (blocks <= 0) return 0;
+    gq_modalix_kernel<TYPE><<<blocks, 256, X::kSmem, s>>>(m);
+    return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+int launch_modalix(int type, const GqModalix& m, void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (type) {
+        case GQ_TYPE_Q4_K: return launch_modalix_t<GQ_TYPE_Q4_K>(m, s);
+        case GQ_TYPE_Q5_K: return launch_modalix_t<GQ_TYPE_Q5_K>(m, s);
+        case GQ_TYPE_Q6_K: return launch_modalix_t<GQ_TYPE_Q6_K>(m, s);
+        case GQ_TYPE_Q8_0: return launch_modalix_t<GQ_TYPE_Q8_0>(m, s);
+        case GQ_TYPE_Q4_0: return launch_modalix_t<GQ_TYPE_Q4_0>(m, s);
+        case GQ_TYPE_Q4_1: return launch_modalix_t<GQ_TYPE_Q4_1>(m, s);
+        case GQ_TYPE_Q5_0: return launch_modalix_t<GQ_TYPE_Q5_0>(m, s);
+        case GQ_TYPE_Q5_1: return launch_modalix_t<GQ_TYPE_Q5_1>(m, s);
+        case GQ_TYPE_Q2_K: return launch_modalix_t<GQ_TYPE_Q2_K>(m, s);
+        case GQ_TYPE_Q3_K: return launch_modalix_t<GQ_TYPE_Q3_K>(m, s);
+        default: return static_cast<int>(cudaErrorInvalidValue);
+    }
 }
 
 int launch_batch(int type, int out_mask, const GqBatch& b, void* stream) {

@@ -6,6 +6,9 @@ hwigo, i.e. (1, 1, I, 1, O), whose memory order is the (I, O) transpose, and, fo
 weights of a padded projection, pads the output channels to a uniform 32-way split with
 zero weights and unit scales.  ``modalix_layout_device`` does this with one kernel pass on
 device-resident outputs; ``modalix_layout`` is the numpy-in, numpy-out form.
+``convert_modalix_device`` / ``modalix_from_gguf`` fuse it with the GGUF conversion itself
+(``gq_convert_modalix``): the GGUF bytes go in, the HWIGO codes and transposed scales come
+out, and the row-major codes never reach memory.
 
 Bundled projections (Phi-3.5 style ``qkv_proj`` / ``gate_up_proj``): ``_build_conv`` looks up
 the bundled tensor when a ``q_proj``/``k_proj``/``v_proj``/``gate_proj``/``up_proj`` weight is
@@ -15,14 +18,16 @@ missing and keeps a range of its output rows (model_graph.py:990-998, 1168-1248)
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 from ml_dtypes import int4
 
 from . import _native as N
 
-__all__ = ["padded_output_channels", "modalix_layout_device", "modalix_layout", "array_partition",
-           "alternate_weight"]
+__all__ = ["padded_output_channels", "modalix_layout_device", "modalix_layout", "convert_modalix_device",
+           "modalix_from_gguf", "array_partition", "alternate_weight"]
 
 MLA_ROW_SIZE = 16   # sima_lmm/utils.py:4
 
@@ -64,6 +69,63 @@ def modalix_layout(scales: np.ndarray, codes: np.ndarray, pad_output: bool = Fal
     w = out_c.cpu().numpy()
     w = w.view(int4) if is_int4 else w
     return out_s.cpu().numpy(), w.reshape(1, 1, codes.shape[1], 1, padded)
+
+
+def convert_modalix_device(fmt: str, src: torch.Tensor, rows: int, cols: int, heads: int = 0,
+                           padded: int | None = None):
+    """GGUF bytes on the GPU -> (scales (cols/B, O') f32, codes (cols, O') int8 or int4 bytes,
+    diagnostics (2,) int32) in the Modalix layout, O' = ``padded`` (default ``rows``),
+    with the llama q/k permutation of ``heads`` heads when ``heads > 0``.
+
+    One pass (``gq_convert_modalix``) when the shape allows it (cols a multiple of 256,
+    rows of whole 16-byte chunks); otherwise the conversion and ``gq_modalix_layout`` run
+    one after the other on the GPU, with the same result."""
+    from .formats import FORMATS
+    f = FORMATS[fmt]
+    if f.block_values == 0:
+        raise TypeError("the Modalix layout writer takes quantized GGUF types")
+    dev = src.device
+    padded = rows if padded is None else padded
+    out_codes = torch.empty((cols, padded), dtype=torch.int8, device=dev)
+    out_scales = torch.empty((cols // f.block_values, padded), dtype=torch.float32, device=dev)
+    diag = torch.zeros(2, dtype=torch.int32, device=dev)
+    rec = N.Tensor()
+    rec.type, rec.perm_heads, rec.rows, rec.cols = f.type_id, heads, rows, cols
+    rec.src, rec.src_bytes = src.data_ptr(), src.numel()
+    rec.codes, rec.scales, rec.diag = out_codes.data_ptr(), out_scales.data_ptr(), diag.data_ptr()
+    stream = torch.cuda.current_stream().cuda_stream
+    st = N.lib().gq_convert_modalix(ctypes.byref(rec), padded, stream)
+    if st == -2:
+        # a shape the fused writer does not take (or a bad size, which the conversion then
+        # reports): convert, then lay out
+        from .device import DeviceTensor, alloc_outputs, convert
+        t = alloc_outputs(DeviceTensor(fmt, rows, cols, src, heads), N.OUT_CODES)
+        convert(t, N.OUT_CODES)
+        s, c = modalix_layout_device(t.scales, t.codes, padded)
+        return s, c, t.diag
+    N.check(st, "gq_convert_modalix")
+    return out_scales, out_codes, diag
+
+
+def modalix_from_gguf(gguf_tensor, heads: int = 0, pad_output: bool = False):
+    """A GGUF reader tensor -> (scales (I/B, O'), weight (1, 1, I, 1, O')) as
+    ``_build_conv`` hands them to ``create_conv_node`` (default reshape, no process
+    functions), O' the int4 32-way padding when ``pad_output``; the requantization warning
+    is logged as the conversion logs it."""
+    from .gguf_conversion import _type_name, requant_warning
+    fmt = _type_name(gguf_tensor.tensor_type)
+    rows, cols = (int(x) for x in gguf_tensor.shape[::-1])
+    is_int4 = fmt == "Q4_0"
+    padded = padded_output_channels(rows, is_int4, pad_output)
+    src = torch.from_numpy(np.ascontiguousarray(gguf_tensor.data).reshape(-1).view(np.uint8)).cuda()
+    s, c, d = convert_modalix_device(fmt, src, rows, cols, heads, padded)
+    w = c.cpu().numpy()
+    w = w.view(np.uint8).view(int4) if is_int4 else w
+    from .formats import FORMATS
+    if FORMATS[fmt].asymmetric:
+        dv = d.cpu().numpy()
+        requant_warning(dv[0:1].view(np.float32)[0], np.int16(dv[1]))
+    return s.cpu().numpy(), w.reshape(1, 1, cols, 1, padded)
 
 
 def array_partition(rows: int, count: int, index: int, span: int) -> tuple[int, int]:

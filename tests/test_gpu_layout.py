@@ -119,3 +119,81 @@ def test_bundled_gate_up_and_float_tensors():
     assert s is None and np.array_equal(b, bias[32:64])
     with pytest.raises(AssertionError):
         load_partition(bt, 7, 0, 1)
+
+
+# ---------------------------------------------------------------------------------------
+# conversion fused with the layout (gq_convert_modalix)
+# ---------------------------------------------------------------------------------------
+
+def _fused_case(fmt, rows, cols, heads=0, padded=None, seed=0, expect_fused=True):
+    import ctypes
+
+    from llima_b200 import _native as N
+    from llima_b200.formats import FORMATS
+    from llima_b200.layout import convert_modalix_device
+    from llima_b200.synth import gen_tensor_bytes
+    from tests.golden_cases import same_bits
+    raw = gen_tensor_bytes(fmt, rows * cols, seed + rows + cols)
+    src = torch.from_numpy(raw.copy()).cuda()
+    padded = rows if padded is None else padded
+    if expect_fused is not None:
+        # whether the one-pass kernel takes this shape (else the wrapper converts, then lays out)
+        f = FORMATS[fmt]
+        rec = N.Tensor()
+        rec.type, rec.perm_heads, rec.rows, rec.cols = f.type_id, heads, rows, cols
+        rec.src, rec.src_bytes = src.data_ptr(), src.numel()
+        oc = torch.empty((cols, padded), dtype=torch.int8, device="cuda")
+        os_ = torch.empty((cols // f.block_values, padded), dtype=torch.float32, device="cuda")
+        rec.codes, rec.scales = oc.data_ptr(), os_.data_ptr()
+        st = N.lib().gq_convert_modalix(ctypes.byref(rec), padded, torch.cuda.current_stream().cuda_stream)
+        assert (st == 0) == expect_fused, (fmt, rows, cols, st)
+    s, c, d = convert_modalix_device(fmt, src, rows, cols, heads, padded)
+    torch.cuda.synchronize()
+    with np.errstate(all="ignore"):
+        s0, w0, dg = O.unpack_tensor(fmt, raw.tobytes(), (rows, cols), log=False)
+    if heads:
+        s0, w0 = O.permute_qk(s0, w0, heads)
+    s2, w2 = O.modalix_layout(s0, w0.view(np.uint8) if fmt == "Q4_0" else w0, padded)
+    got_c = c.cpu().numpy().view(np.uint8)
+    assert got_c.shape == (cols, padded)
+    assert np.array_equal(got_c, w2.reshape(cols, padded).view(np.uint8)), (fmt, rows, cols, heads)
+    assert same_bits(s.cpu().numpy(), s2), (fmt, rows, cols, heads)
+    if dg is not None:
+        from llima_b200.device import diag_values
+        r, cl = diag_values(d)
+        assert same_bits(np.float32(r), np.float32(dg.round_error)) and int(cl) == int(dg.clip_error)
+
+
+@pytest.mark.parametrize("fmt,cols", [("Q4_K", 4096), ("Q5_K", 1024), ("Q6_K", 2048), ("Q8_0", 512),
+                                      ("Q4_0", 256), ("Q4_1", 512), ("Q5_0", 256), ("Q5_1", 768),
+                                      ("Q2_K", 1024), ("Q3_K", 2048)])
+@pytest.mark.parametrize("rows", [128, 300, 37, 1])
+def test_fused_layout_matches_oracle(fmt, cols, rows):
+    _fused_case(fmt, rows, cols)
+
+
+@pytest.mark.parametrize("fmt,rows,cols,heads", [("Q4_K", 256, 1024, 2), ("Q4_K", 512, 512, 2),
+                                                 ("Q6_K", 256, 2048, 8), ("Q8_0", 192, 256, 6),
+                                                 ("Q4_K", 4096, 4096, 32), ("Q4_K", 1024, 4096, 8)])
+def test_fused_layout_with_head_permutation(fmt, rows, cols, heads):
+    # head dims 128, 256 (a head spans two tiles), 32, 32; the Llama-3-8B attn_q / attn_k
+    _fused_case(fmt, rows, cols, heads)
+
+
+@pytest.mark.parametrize("fmt,rows,padded", [("Q4_0", 528, 544), ("Q4_0", 1040, 1056), ("Q4_K", 300, 320)])
+def test_fused_layout_output_padding(fmt, rows, padded):
+    _fused_case(fmt, rows, 512, padded=padded)
+
+
+@pytest.mark.parametrize("fmt,rows,cols", [("Q8_0", 40, 96), ("Q6_K", 64, 256), ("Q3_K", 16, 768),
+                                           ("Q2_K", 8, 512)])
+def test_fused_layout_unsupported_shapes_fall_back(fmt, rows, cols):
+    # cols not a multiple of 256, or rows that do not start on 16-byte boundaries: the
+    # wrapper converts, then lays out, with the same result
+    _fused_case(fmt, rows, cols, expect_fused=False)
+
+
+def test_fused_layout_full_size_llama_ffn():
+    # Llama-3-8B ffn_gate (Q4_K 14336 x 4096) and ffn_down (Q6_K 4096 x 14336)
+    _fused_case("Q4_K", 14336, 4096)
+    _fused_case("Q6_K", 4096, 14336)
