@@ -599,6 +599,9 @@ def main():
         print(json.dumps(line), flush=True)
         return 0
 
+    # stdout carries exactly one JSON line: NCCL's own log lines (printed when NCCL_DEBUG is
+    # set) go to stderr unless the caller chose a file for them
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     import torch
     import torch.distributed as dist
     if world > 1:
