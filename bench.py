@@ -571,6 +571,15 @@ def run_ours(args, rank, world, local_rank):
 
 def main():
     args = parse_args()
+    # stdout carries exactly one JSON line: everything else any library writes to file
+    # descriptor 1 (NCCL's version banner, for one) goes to stderr, and the result line is
+    # written to the original stdout
+    json_fd = os.dup(1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
+
+    def emit(line: dict) -> None:
+        os.write(json_fd, (json.dumps(line) + "\n").encode())
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -596,12 +605,9 @@ def main():
                 "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                                  "sample": sample},
                 "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        emit(line)
         return 0
 
-    # stdout carries exactly one JSON line: NCCL's own log lines (printed when NCCL_DEBUG is
-    # set) go to stderr unless the caller chose a file for them
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     import torch
     import torch.distributed as dist
     if world > 1:
@@ -621,7 +627,7 @@ def main():
         line = run_ours(args, rank, world, local_rank)
         if rank == 0 and line is not None:
             line["cpu_baseline"] = cpu
-            print(json.dumps(line), flush=True)
+            emit(line)
     finally:
         if world > 1 and dist.is_initialized():
             dist.destroy_process_group()
