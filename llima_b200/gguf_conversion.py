@@ -239,17 +239,42 @@ class GgufReaderProxy:
         return info
 
 
+def _rebuild_model(gguf_module: str, cls_module: str, qualname: str, state: dict):
+    """Unpickle a ``GgufModel`` (or subclass) in a worker process: install the B200 path
+    into the worker's fresh import of the reference module first, so that the model's
+    ``__setstate__`` reopens the file through this module's ``GgufReaderProxy`` and its
+    ``load_weight`` converts on the GPU."""
+    import importlib
+    install(importlib.import_module(gguf_module))
+    cls = importlib.import_module(cls_module)
+    for part in qualname.split("."):
+        cls = getattr(cls, part)
+    obj = cls.__new__(cls)
+    obj.__setstate__(state)
+    return obj
+
+
 def install(module=None):
     """Route an imported ``sima_lmm.gguf.gguf_conversion`` through the B200 path.
 
     Replaces the module's ``unpack_gguf_tensor`` and ``GgufReaderProxy`` and makes
     ``GgufModel.load_weight`` apply the llama q/k permutation inside the decode instead
-    of on the host afterwards.  Returns the module."""
+    of on the host afterwards.  ``GgufModel`` objects pickled for the reference's spawned
+    compile workers (``sima_lmm/model/base.py:665-709``) carry the installation with them:
+    they unpickle through ``_rebuild_model``, which installs the path in the worker before
+    restoring the object.  Returns the module."""
     if module is None:
         import sima_lmm.gguf.gguf_conversion as module  # noqa: PLC0415 (reference package)
     module.unpack_gguf_tensor = unpack_gguf_tensor
     module.GgufReaderProxy = GgufReaderProxy
     model_cls = module.GgufModel
+    module_name = module.__name__
+
+    def __reduce_ex__(self, protocol):
+        cls = type(self)
+        return (_rebuild_model, (module_name, cls.__module__, cls.__qualname__, self.__getstate__()))
+
+    model_cls.__reduce_ex__ = __reduce_ex__
 
     def load_weight(self, name: str, is_hf_name: bool = True, force_float: bool = False):
         if is_hf_name:

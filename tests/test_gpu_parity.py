@@ -241,6 +241,35 @@ def test_host_path_pinned_and_pageable_buffers(layout):
         N.lib().gq_session_destroy(sess)
 
 
+@pytest.mark.parametrize("layout", ["row_slice", "fortran", "step"])
+def test_unpack_gguf_tensor_non_contiguous_views(layout):
+    """A reader tensor whose data is not one contiguous block (rows cut out of a wider
+    buffer, Fortran order, every other row of an interleaved buffer): the result equals
+    the oracle on the same bytes."""
+    import types
+    from llima_b200.gguf_conversion import unpack_gguf_tensor
+    fmt, rows, cols = "Q4_K", 64, 512
+    raw = gen_tensor_bytes(fmt, rows * cols, 91)
+    rb = raw.size // rows
+    if layout == "row_slice":
+        wide = np.zeros((rows, rb + 48), dtype=np.uint8)
+        wide[:, :rb] = raw.reshape(rows, rb)
+        data = wide[:, :rb]
+    elif layout == "fortran":
+        data = np.asfortranarray(raw.reshape(rows, rb))
+    else:
+        both = np.zeros((2 * rows, rb), dtype=np.uint8)
+        both[::2] = raw.reshape(rows, rb)
+        data = both[::2]
+    assert not data.flags.c_contiguous
+    t = types.SimpleNamespace(tensor_type=FORMATS[fmt].type_id, data=data,
+                              shape=np.array([cols, rows], dtype=np.uint64))
+    s, w = unpack_gguf_tensor(t, False)
+    with np.errstate(all="ignore"):
+        s2, w2, _ = O.unpack_tensor(fmt, raw.tobytes(), (rows, cols), log=False)
+    assert same_bits(w, w2) and same_bits(s, s2)
+
+
 def test_unpack_gguf_tensor_dropin_reader(tmp_path):
     gguf = pytest.importorskip("gguf")
     from llima_b200.gguf_conversion import GgufReaderProxy
