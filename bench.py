@@ -621,9 +621,14 @@ def main():
             cores = host_cores()
             gbs, total, wall = cpu_throughput(args.model, args.seed, cores, sample_mb=8.0,
                                               seconds=args.cpu_seconds)
+            # and one process alone, as the reference runs without its process pool
+            gbs1, total1, wall1 = cpu_throughput(args.model, args.seed, 1, sample_mb=8.0,
+                                                 seconds=max(2.0, args.cpu_seconds / 2))
             cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                    "sample": f"{cores} spawned workers, each an 8 MB slice of the {args.model} format mix "
-                             f"converted repeatedly for {args.cpu_seconds:.0f} s ({total / 1e9:.2f} GB in {wall:.1f} s)"}
+                             f"converted repeatedly for {args.cpu_seconds:.0f} s ({total / 1e9:.2f} GB in {wall:.1f} s)",
+                   "value_1_process": round(gbs1, 4),
+                   "sample_1_process": f"1 spawned worker, the same 8 MB slice, {total1 / 1e9:.2f} GB in {wall1:.1f} s"}
         line = run_ours(args, rank, world, local_rank)
         if rank == 0 and line is not None:
             line["cpu_baseline"] = cpu
