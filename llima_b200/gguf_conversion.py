@@ -16,6 +16,7 @@ reference module so that ``GgufModel`` and everything above it run unchanged.
 from __future__ import annotations
 
 import ctypes
+import functools
 import logging
 import mmap
 import os
@@ -259,7 +260,9 @@ def install(module=None):
 
     Replaces the module's ``unpack_gguf_tensor`` and ``GgufReaderProxy`` and makes
     ``GgufModel.load_weight`` apply the llama q/k permutation inside the decode instead
-    of on the host afterwards.  ``GgufModel`` objects pickled for the reference's spawned
+    of on the host afterwards, and ``GgufModel.model_config`` reads the vocabulary size
+    from the token embedding's header instead of decoding it.  ``GgufModel`` objects pickled
+    for the reference's spawned
     compile workers (``sima_lmm/model/base.py:665-709``) carry the installation with them:
     they unpickle through ``_rebuild_model``, which installs the path in the worker before
     restoring the object.  Returns the module."""
@@ -276,9 +279,31 @@ def install(module=None):
 
     model_cls.__reduce_ex__ = __reduce_ex__
 
+    # model_config decodes the whole token embedding only to read the vocabulary size
+    # (gguf_conversion.py:436-437): while it runs, that one load returns an array of the
+    # tensor's shape with no columns, read from the tensor's header
+    prop = model_cls.__dict__.get("model_config")
+    if isinstance(prop, functools.cached_property) and not getattr(prop.func, "_llima_b200", False):
+        compute = prop.func
+
+        def model_config(self):
+            self._llima_b200_shape_only = True
+            try:
+                return compute(self)
+            finally:
+                self.__dict__.pop("_llima_b200_shape_only", None)
+
+        model_config._llima_b200 = True
+        model_config.__doc__ = compute.__doc__
+        wrapped = functools.cached_property(model_config)
+        wrapped.__set_name__(model_cls, "model_config")
+        model_cls.model_config = wrapped
+
     def load_weight(self, name: str, is_hf_name: bool = True, force_float: bool = False):
         if is_hf_name:
             name = self.convert_hf_weight_name(name)
+        if name == "token_embd.weight" and self.__dict__.get("_llima_b200_shape_only"):
+            return None, np.empty((int(self.tensor_info[name]["shape"][0]), 0), dtype=np.float32)
         heads = 0
         if self._need_permute_qk_proj:
             if name.endswith(("attn_q.weight", "attn_q.bias")):

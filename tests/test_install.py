@@ -111,7 +111,7 @@ def test_install_follows_the_model_into_spawned_workers(tmp_path):
     assert model._need_permute_qk_proj
     from llima_b200.gguf_conversion import install
     saved = (gc.unpack_gguf_tensor, gc.GgufReaderProxy, gc.GgufModel.load_weight,
-             gc.GgufModel.__dict__.get("__reduce_ex__"))
+             gc.GgufModel.__dict__.get("__reduce_ex__"), gc.GgufModel.__dict__["model_config"])
     try:
         install(gc)
         data = pickle.dumps(model)
@@ -124,6 +124,37 @@ def test_install_follows_the_model_into_spawned_workers(tmp_path):
             del gc.GgufModel.__reduce_ex__
         else:
             gc.GgufModel.__reduce_ex__ = saved[3]
+
+
+def test_installed_model_config_skips_the_embedding_decode(tmp_path, monkeypatch):
+    """After install, building a GgufModel reads the vocabulary size from the token
+    embedding's header: the config equals the reference's, and no tensor is converted
+    (the conversion is made to fail to prove it)."""
+    gc = _import_reference()
+    path = tmp_path / "tiny.gguf"
+    _write_gguf(path)
+    want = gc.GgufModel(path).model_config      # the reference's own path
+    from llima_b200 import gguf_conversion as G
+    saved = (gc.unpack_gguf_tensor, gc.GgufReaderProxy, gc.GgufModel.load_weight,
+             gc.GgufModel.__dict__.get("__reduce_ex__"), gc.GgufModel.__dict__["model_config"])
+
+    def no_conversion(*a, **k):
+        raise AssertionError("a tensor was converted while building the config")
+
+    monkeypatch.setattr(G, "convert_host", no_conversion)
+    try:
+        G.install(gc)
+        G.install(gc)                            # a second install wraps nothing twice
+        model = gc.GgufModel(path)
+        assert model.model_config == want and model.model_config["vocab_size"] == 64
+        assert "_llima_b200_shape_only" not in model.__dict__
+    finally:
+        gc.unpack_gguf_tensor, gc.GgufReaderProxy, gc.GgufModel.load_weight = saved[:3]
+        if saved[3] is None:
+            del gc.GgufModel.__reduce_ex__
+        else:
+            gc.GgufModel.__reduce_ex__ = saved[3]
+        gc.GgufModel.model_config = saved[4]
 
 
 # ---------------------------------------------------------------------------------------
