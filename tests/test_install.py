@@ -124,6 +124,7 @@ def test_install_follows_the_model_into_spawned_workers(tmp_path):
             del gc.GgufModel.__reduce_ex__
         else:
             gc.GgufModel.__reduce_ex__ = saved[3]
+        gc.GgufModel.model_config = saved[4]
 
 
 def test_installed_model_config_skips_the_embedding_decode(tmp_path, monkeypatch):
