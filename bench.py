@@ -453,6 +453,41 @@ def run_ours(args, rank, world, local_rank):
                        "launches_per_step": len(mrecs), "api": "gq_convert_modalix (CUDA graph of per-tensor launches)"}
         del mrecs, lrecs
 
+    # ---- token-embedding rows for the runtime (gq_embedding_rows: force_float dequantize,
+    # x embed_scale, bf16 round, per-row int8 with a bf16 scale), on this rank's piece of
+    # token_embd; traffic = GGUF bytes read + int8 codes + bf16 row scales written
+    embedding = None
+    if not args.no_modalix and out_mask == N.OUT_CODES:
+        emb = [t for t in tensors if t.name == "token_embd.weight"]
+        if emb:
+            t = emb[0]
+            f = FORMATS[t.fmt]
+            codes_e = torch.empty((t.rows, t.cols), dtype=torch.int8, device=dev)
+            scales_e = torch.empty((t.rows, 1), dtype=torch.uint16, device=dev)
+
+            def estep():
+                N.check(N.lib().gq_embedding_rows(f.type_id, t.src.data_ptr(), t.src.numel(), t.rows, t.cols, 1.0, 1,
+                                                  codes_e.data_ptr(), scales_e.data_ptr(), None,
+                                                  torch.cuda.current_stream().cuda_stream), "gq_embedding_rows")
+
+            for _ in range(3):
+                estep()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                estep()
+            e1.record()
+            torch.cuda.synchronize()
+            e_ms = e0.elapsed_time(e1) / 20
+            peak_, _ = measured_peak()
+            moved = t.src_bytes + t.rows * t.cols + 2 * t.rows
+            embedding = {"value": round(t.src_bytes / (e_ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms": round(e_ms, 4),
+                         "rows": t.rows, "cols": t.cols, "format": t.fmt,
+                         "hbm_frac": round(moved / (e_ms / 1e3) / 1e9 / peak_, 4), "rank": rank,
+                         "api": "gq_embedding_rows on this rank's token_embd rows (quantize=1)"}
+            del codes_e, scales_e
+
     # ---- end to end through the C ABI host-buffer call (pinned host memory)
     e2e = None
     if not args.no_e2e and args.e2e_steps > 0:
@@ -564,7 +599,7 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded, BASELINE distributions)",
         "config": workload_config(args, world),
         "roofline": roofline, "gpu_launches": launches_per_step * args.steps, "diag_written": bool(tot[2].item() == world),
-        "e2e": e2e, "clocks": clocks, "modalix_fused": modalix,
+        "e2e": e2e, "clocks": clocks, "modalix_fused": modalix, "embedding_rows": embedding,
     }
     return line
 

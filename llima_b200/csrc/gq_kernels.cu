@@ -908,7 +908,7 @@ struct MxFmt {
     static constexpr int kTBytes = kModalixCols * kModalixRows;   // column tile (bytes)
     static constexpr int kRBytes = kModalixRows * kModalixCols;   // row tile
     static constexpr int kSBytes = kModalixRows * 16 * 4;         // scale tile (up to 16 per row)
-    static constexpr int kSmem = kTBytes + kRBytes + kSBytes + 8 * kWarpStaging + 1024;   // + alignment
+    static constexpr int kSmem = kTBytes + kRBytes + kSBytes + 8 * kWarpStaging + 4096;   // + alignment
 };
 
 // Source row of output channel o (inverse of the q/k permutation of
@@ -928,8 +928,9 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
     extern __shared__ __align__(16) uint8_t smem_raw[];
     __shared__ float recip[17];
     if (threadIdx.x < 17) recip[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, static_cast<float>(threadIdx.x)) : 0.0f;
-    // the tiles start on a 1 KiB boundary (the row tile's swizzle works on 256-byte blocks)
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // the tiles start on a 4 KiB boundary: the row tile's swizzle key (shared-address bits
+    // 8..11) is then the row index mod 16
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 4095) & ~uintptr_t(4095));
     uint8_t* rtile = smem + X::kTBytes;                                        // 128 rows x 256 bytes
     float* stile = reinterpret_cast<float*>(smem + X::kTBytes + X::kRBytes);   // 128 rows x NBS
     const uint32_t t_s = smem_u32addr(smem);                                   // 256 rows x 32 words
@@ -1013,24 +1014,37 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
             }
         }
         __syncthreads();
-        // phase B: the next tile's copies go out; transpose codes into the column tile
-        // (word a of column-tile row 4b + k at a ^ (b & 31)); scales straight out
+        // phase B: the next tile's copies go out; transpose codes into the column tile.  A
+        // thread takes 16 output channels (rows 16a..16a+15 of the row tile) x 4 input
+        // channels (4b..4b+3): 4x4-byte blocks swapped by PRMT, and each input channel's 16
+        // bytes stored at chunk a ^ (b & 7) of its 128-byte column-tile row
         issue(t + gridDim.x);
-#pragma unroll 2
-        for (int it = 0; it < 8; ++it) {
-            const int a = warp + 8 * (it >> 1);       // output channels 4a..4a+3
-            const int b = lane + 32 * (it & 1);       // input channels 4b..4b+3
-            uint32_t x[4];
+        const bool full = valid_rows == kModalixRows;
+#pragma unroll 1
+        for (int it = 0; it < 2; ++it) {
+            const int a = warp;
+            const int b = lane + 32 * it;
+            uint32_t y[4][4];   // [row group j][input channel k]
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                x[j] = (4 * a + j < valid_rows) ? lds_u32(row_swizzle(r_s + (4 * a + j) * 256 + 4 * b)) : 0u;
-            const uint32_t t0 = __byte_perm(x[0], x[1], 0x5140), t1 = __byte_perm(x[0], x[1], 0x7362);
-            const uint32_t t2 = __byte_perm(x[2], x[3], 0x5140), t3 = __byte_perm(x[2], x[3], 0x7362);
-            const uint32_t tw = t_s + 4 * (b * 128 + (a ^ (b & 31)));
-            sts(tw, __byte_perm(t0, t2, 0x5410));
-            sts(tw + 128, __byte_perm(t0, t2, 0x7632));
-            sts(tw + 256, __byte_perm(t1, t3, 0x5410));
-            sts(tw + 384, __byte_perm(t1, t3, 0x7632));
+            for (int j = 0; j < 4; ++j) {
+                uint32_t x[4];
+#pragma unroll
+                for (int mm = 0; mm < 4; ++mm) {
+                    const int r = 16 * a + 4 * j + mm;   // r % 16 = 4j + mm: the swizzle key
+                    const uint32_t addr = r_s + r * 256 + ((((b >> 2) ^ (4 * j + mm)) << 4) | ((b & 3) << 2));
+                    x[mm] = (full || r < valid_rows) ? lds_u32(addr) : 0u;
+                }
+                const uint32_t t0 = __byte_perm(x[0], x[1], 0x5140), t1 = __byte_perm(x[0], x[1], 0x7362);
+                const uint32_t t2 = __byte_perm(x[2], x[3], 0x5140), t3 = __byte_perm(x[2], x[3], 0x7362);
+                y[j][0] = __byte_perm(t0, t2, 0x5410);
+                y[j][1] = __byte_perm(t0, t2, 0x7632);
+                y[j][2] = __byte_perm(t1, t3, 0x5410);
+                y[j][3] = __byte_perm(t1, t3, 0x7632);
+            }
+            const uint32_t chunk = static_cast<uint32_t>(a ^ (b & 7)) << 4;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                sts(t_s + (4 * b + k) * 128 + chunk, make_uint4(y[0][k], y[1][k], y[2][k], y[3][k]));
         }
         const int64_t rp = m.rows_padded;
         for (int task = threadIdx.x; task < X::NBS * 32; task += 256) {
@@ -1052,26 +1066,22 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
         // phase C: column tile -> codes, 16 output channels per lane
         const int q = lane & 7;                                               // output channels 16q..16q+15
         const int64_t o0 = d0 + 16 * q;
-        const bool full = o0 + 16 <= rp;
-#pragma unroll 2
-        for (int it = 0; it < 8; ++it) {
-            const int idx = warp * 8 + it;
-            const int i = 16 * (idx >> 2) + (idx & 3) + 4 * (lane >> 3);   // input channel in the tile
-            if (o0 >= rp) continue;
-            const uint32_t rowa = t_s + 128 * i;
-            const int sw = (i >> 2) & 31;
-            uint4 w;
-            w.x = lds_u32(rowa + 4 * ((4 * q + 0) ^ sw));
-            w.y = lds_u32(rowa + 4 * ((4 * q + 1) ^ sw));
-            w.z = lds_u32(rowa + 4 * ((4 * q + 2) ^ sw));
-            w.w = lds_u32(rowa + 4 * ((4 * q + 3) ^ sw));
-            uint8_t* dst = m.out_codes + static_cast<int64_t>(cb * kModalixCols + i) * rp + o0;
-            if (full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                stg128(dst, w);
-            } else {
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-                for (int e = 0; e < 16 && o0 + e < rp; ++e)
-                    st_global(dst + e, static_cast<uint8_t>(ws[e >> 2] >> (8 * (e & 3))));
+        const bool seg_full = o0 + 16 <= rp;
+        if (o0 < rp) {
+#pragma unroll 4
+            for (int it = 0; it < 8; ++it) {
+                const int idx = warp * 8 + it;
+                const int i = 16 * (idx >> 2) + (idx & 3) + 4 * (lane >> 3);   // input channel in the tile
+                const uint4 w = lds_v4(t_s + i * 128 + ((q ^ ((i >> 2) & 7)) << 4));
+                uint8_t* dst = m.out_codes + static_cast<int64_t>(cb * kModalixCols + i) * rp + o0;
+                if (seg_full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    stg128(dst, w);
+                } else {
+                    for (int e = 0; e < 16 && o0 + e < rp; ++e) {
+                        const uint32_t word = e < 4 ? w.x : (e < 8 ? w.y : (e < 12 ? w.z : w.w));
+                        st_global(dst + e, static_cast<uint8_t>(word >> (8 * (e & 3))));
+                    }
+                }
             }
         }
     }

@@ -50,6 +50,40 @@ def test_fused_embedding_rows_match_oracle(fmt, rows, cols, embed_scale):
     assert np.array_equal(values.cpu().numpy().view(np.uint32), v.view(np.uint32))
 
 
+@pytest.mark.parametrize("fmt,rows,cols", [("Q6_K", 200, 2048), ("Q4_K", 150, 1024), ("Q5_K", 100, 1024),
+                                           ("Q8_0", 300, 512), ("Q4_0", 300, 512)])
+@pytest.mark.parametrize("embed_scale", [1.0, 3.0e38, float("inf")])
+def test_fused_embedding_rows_nonfinite_and_extreme(fmt, rows, cols, embed_scale):
+    """Uniform random bytes (NaN, inf and huge f16 constants in some blocks), a scale that
+    overflows, and an infinite scale: every row quantizes as the oracle does (rows whose
+    absmax is not finite get zero codes and a non-finite scale)."""
+    from llima_b200.formats import FORMATS
+    f = FORMATS[fmt]
+    n_units = rows * cols // f.unit_values
+    raw = np.frombuffer(np.random.default_rng(rows + cols).bytes(n_units * f.unit_bytes), dtype=np.uint8).copy()
+    src = torch.from_numpy(raw.copy()).cuda()
+    codes, scales = embedding_rows_device(fmt, src, rows, cols, embed_scale, True)
+    torch.cuda.synchronize()
+    q, s = _oracle_fused(fmt, raw, rows, cols, embed_scale, True)
+    assert np.array_equal(codes.cpu().numpy(), q)
+    got, want = scales.cpu().numpy(), s.view(np.uint16)
+    nan = np.isnan(got.view(bfloat16).astype(np.float32)) & np.isnan(want.view(bfloat16).astype(np.float32))
+    assert np.all(nan | (got == want))
+
+
+@pytest.mark.parametrize("fmt", ["Q6_K", "Q4_K", "Q8_0"])
+def test_fused_embedding_rows_half_integer_quotients(fmt):
+    """Rows where many y / step land exactly on half-integers (y = absmax * k / 254 in
+    bf16), so rint's ties are decided by the exactly divided quotient."""
+    rows, cols = 64, 1024
+    raw = _raw(fmt, rows, cols, 7)
+    src = torch.from_numpy(raw.copy()).cuda()
+    codes, scales = embedding_rows_device(fmt, src, rows, cols, 2.0, True)
+    torch.cuda.synchronize()
+    q, s = _oracle_fused(fmt, raw, rows, cols, 2.0, True)
+    assert np.array_equal(codes.cpu().numpy(), q) and np.array_equal(scales.cpu().numpy(), s.view(np.uint16))
+
+
 def test_quantize_rows_match_oracle_with_zero_rows():
     rng = np.random.default_rng(3)
     x = rng.normal(0, 0.1, (300, 1024)).astype(np.float32).astype(bfloat16).astype(np.float32)
