@@ -2,8 +2,13 @@
 // host-buffer session that pipelines host->device copies, kernels and device->host copies.
 #include <cuda_runtime.h>
 
+#include <sys/mman.h>
+#include <unistd.h>
+
 #include <algorithm>
 #include <atomic>
+#include <cerrno>
+#include <deque>
 #include <condition_variable>
 #include <cstdlib>
 #include <cstring>
@@ -383,7 +388,7 @@ int gq_quantize_rows(const float* x, int64_t rows, int64_t cols, int8_t* codes, 
 // ---------------------------------------------------------------------------------------
 // Host-buffer session
 //
-// A request is cut into pieces of about kPieceTarget bytes of device footprint (input +
+// A request is cut into pieces of about piece_target() bytes of device footprint (input +
 // outputs; a permuted tensor stays whole), and the pieces rotate through kSlots device
 // slots, each with its own stream.  Pinned host buffers are copied by the DMA engines
 // directly.  A pageable one (a numpy array, the memory map of a GGUF file) is bounced
@@ -397,7 +402,19 @@ int gq_quantize_rows(const float* x, int64_t rows, int64_t cols, int8_t* codes, 
 namespace {
 
 constexpr int kSlots = 3;
-constexpr size_t kPieceTarget = size_t(32) << 20;
+constexpr size_t kPieceTargetDefault = size_t(64) << 20;
+
+// Slot footprint of one piece (LLIMA_B200_PIECE_MB overrides; at least 1 MiB).
+size_t piece_target() {
+    static const size_t v = [] {
+        if (const char* e = std::getenv("LLIMA_B200_PIECE_MB")) {
+            const long mb = std::atol(e);
+            if (mb >= 1) return static_cast<size_t>(mb) << 20;
+        }
+        return kPieceTargetDefault;
+    }();
+    return v;
+}
 constexpr size_t kCopyChunk = size_t(2) << 20;
 
 struct CopyJob {
@@ -484,6 +501,79 @@ class CopyPool {
     bool stop_ = false;
 };
 
+// Background threads that fault in the pages of pageable result buffers ahead of the copies
+// that fill them (madvise MADV_POPULATE_WRITE: the kernel maps and zeroes the pages, and
+// never changes the content of a page that is already there, so it can run beside the
+// copies).  Fresh result arrays otherwise take one page fault per page inside those copies,
+// which bounds the host side of a pageable request.  Kernels without the advice (before
+// Linux 5.14) refuse it and nothing is done.
+class PrefaultPool {
+  public:
+    explicit PrefaultPool(int threads) {
+        for (int i = 0; i < threads; ++i) workers_.emplace_back([this] { work(); });
+    }
+    ~PrefaultPool() {
+        {
+            std::lock_guard<std::mutex> g(mu_);
+            stop_ = true;
+            q_.clear();
+        }
+        cv_.notify_all();
+        for (auto& t : workers_) t.join();
+    }
+    // Queue [p, p + bytes) (whole pages inside it), in order.
+    void submit(void* p, size_t bytes) {
+        const uintptr_t page = static_cast<uintptr_t>(sysconf(_SC_PAGESIZE));
+        uintptr_t a = (reinterpret_cast<uintptr_t>(p) + page - 1) & ~(page - 1);
+        const uintptr_t end = (reinterpret_cast<uintptr_t>(p) + bytes) & ~(page - 1);
+        std::lock_guard<std::mutex> g(mu_);
+        if (stop_ || unsupported_.load()) return;
+        for (; a < end; a += kChunk) q_.push_back({a, std::min<uintptr_t>(kChunk, end - a)});
+        cv_.notify_all();
+    }
+    // Drop what has not started and wait for what has (the buffers may be freed next).
+    void cancel() {
+        std::unique_lock<std::mutex> g(mu_);
+        q_.clear();
+        idle_.wait(g, [&] { return active_ == 0; });
+    }
+
+  private:
+    static constexpr uintptr_t kChunk = uintptr_t(8) << 20;
+    struct Range {
+        uintptr_t a, n;
+    };
+    void work() {
+        for (;;) {
+            Range r;
+            {
+                std::unique_lock<std::mutex> g(mu_);
+                cv_.wait(g, [&] { return stop_ || !q_.empty(); });
+                if (stop_) return;
+                r = q_.front();
+                q_.pop_front();
+                ++active_;
+            }
+#ifdef MADV_POPULATE_WRITE
+            if (madvise(reinterpret_cast<void*>(r.a), r.n, MADV_POPULATE_WRITE) != 0 && errno == EINVAL)
+                unsupported_.store(true);
+#endif
+            {
+                std::lock_guard<std::mutex> g(mu_);
+                --active_;
+            }
+            idle_.notify_all();
+        }
+    }
+    std::vector<std::thread> workers_;
+    std::mutex mu_;
+    std::condition_variable cv_, idle_;
+    std::deque<Range> q_;
+    int active_ = 0;
+    bool stop_ = false;
+    std::atomic<bool> unsupported_{false};
+};
+
 int copy_threads() {
     if (const char* e = std::getenv("LLIMA_B200_COPY_THREADS")) {
         const int n = std::atoi(e);
@@ -517,6 +607,7 @@ struct gq_session {
     gq_diag_t* d_diag = nullptr;
     int diag_cap = 0;
     std::unique_ptr<CopyPool> pool;
+    std::unique_ptr<PrefaultPool> prefault;
     std::mutex mu;                  // one gq_convert_host at a time per session
 };
 
@@ -567,7 +658,8 @@ bool ensure_bounce(gq_session* s) {
         }
     }
     if (!s->pool) s->pool.reset(new (std::nothrow) CopyPool(copy_threads()));
-    return s->pool != nullptr;
+    if (!s->prefault) s->prefault.reset(new (std::nothrow) PrefaultPool(std::max(1, copy_threads() / 2)));
+    return s->pool != nullptr && s->prefault != nullptr;
 }
 
 }  // namespace
@@ -606,6 +698,7 @@ int gq_session_destroy(gq_session_t* s) {
         if (s->stream[i]) cudaStreamSynchronize(s->stream[i]);
     }
     s->pool.reset();
+    s->prefault.reset();
     for (int i = 0; i < kSlots; ++i) {
         if (s->done[i]) cudaEventDestroy(s->done[i]);
         if (s->stream[i]) cudaStreamDestroy(s->stream[i]);
@@ -668,6 +761,7 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
     auto fail = [&](int e) {
         for (int k = 0; k < kSlots; ++k) cudaStreamSynchronize(s->stream[k]);
         cudaGetLastError();
+        if (s->prefault) s->prefault->cancel();
         return e;
     };
 
@@ -689,9 +783,9 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
         for (int k = 1; k < kSlots; ++k) cudaStreamWaitEvent(s->stream[k], s->done[0], 0);
     }
 
-    // Cut the work into pieces of about kPieceTarget bytes of slot footprint: large
+    // Cut the work into pieces of about piece_target() bytes of slot footprint: large
     // tensors are split on unit boundaries, small ones are packed together.
-    const size_t target = std::min(s->slot_bytes, kPieceTarget);
+    const size_t target = std::min(s->slot_bytes, piece_target());
     std::vector<std::vector<Member>> pieces;
     {
         std::vector<Member> cur;
@@ -723,6 +817,25 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
             }
         }
         if (!cur.empty()) pieces.push_back(std::move(cur));
+    }
+
+    // pageable result buffers: fault their pages in ahead of the copies, piece by piece
+    if (s->prefault && std::find(bounce_out.begin(), bounce_out.end(), 1) != bounce_out.end()) {
+        for (const auto& piece : pieces) {
+            for (const Member& m : piece) {
+                if (!bounce_out[m.tensor]) continue;
+                const gq_tensor_t& t = tensors[m.tensor];
+                const TypeInfo& ti = info[m.tensor];
+                const size_t nvals = static_cast<size_t>(m.units) * ti.unit_values;
+                if (ti.block_values == 0) {
+                    s->prefault->submit(static_cast<uint8_t*>(static_cast<void*>(t.values)) + m.unit0 * ti.unit_bytes,
+                                        nvals * ti.unit_bytes);
+                    continue;
+                }
+                if (out_mask & GQ_OUT_CODES) s->prefault->submit(static_cast<uint8_t*>(t.codes) + m.unit0 * ti.unit_values, nvals);
+                if (out_mask & GQ_OUT_F32) s->prefault->submit(t.values + m.unit0 * ti.unit_values, 4 * nvals);
+            }
+        }
     }
 
     struct Copy {
@@ -839,6 +952,7 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
         st = cuda_status(cudaStreamSynchronize(s->stream[k]));
         if (st != GQ_OK) return fail(st);
     }
+    if (s->prefault) s->prefault->cancel();
     if (host_diags != nullptr && count > 0) {
         // every stream's kernels have finished: read the maxima
         st = cuda_status(cudaMemcpy(host_diags, s->d_diag, sizeof(gq_diag_t) * count, cudaMemcpyDeviceToHost));
