@@ -215,11 +215,15 @@ GQ_API int gq_embedding_rows(int32_t type, const void* src, size_t src_bytes, in
 GQ_API int gq_quantize_rows(const float* x, int64_t rows, int64_t cols, int8_t* codes, uint16_t* scales_bf16,
                             void* stream);
 
-/* Host-buffer path: an opaque per-device session owning device staging memory and
- * streams.  gq_convert_host copies each tensor's bytes host->device, converts and copies
- * the results device->host, pipelining tensors (and pieces of large tensors) across two
- * staging slots; host buffers may be pinned (fastest) or pageable.  The pointers in
- * `tensors` are HOST pointers; diags (optional, host, one per tensor) receive the maxima. */
+/* Host-buffer path: an opaque per-device session owning device staging memory, streams
+ * and (on first use with pageable buffers) pinned bounce slots and host copy threads.
+ * gq_convert_host copies each tensor's bytes host->device, converts and copies the results
+ * device->host, pipelining pieces (of about 64 MB; permuted tensors in whole heads, one
+ * head must fit `staging_bytes`) across three staging slots; host buffers may be pinned
+ * (copied directly) or pageable (bounced through the pinned slots).  The pointers in
+ * `tensors` are HOST pointers; diags (optional, host, one per tensor) receive the maxima.
+ * Calls on one session are serialized.  A session belongs to the process that created it
+ * (a forked child creates its own). */
 typedef struct gq_session gq_session_t;
 GQ_API int gq_session_create(int32_t device, size_t staging_bytes, gq_session_t** out);
 GQ_API int gq_session_destroy(gq_session_t* session);

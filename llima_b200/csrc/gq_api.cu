@@ -738,9 +738,11 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
             if ((out_mask & GQ_OUT_CODES) && (t.codes == nullptr || t.scales == nullptr)) return GQ_ERR_NULL;
             if ((out_mask & GQ_OUT_F32) && t.values == nullptr) return GQ_ERR_NULL;
         }
-        // a permuted tensor moves rows across its whole extent: it must fit one slot
+        // a permuted tensor is cut into whole heads (the permutation keeps them apart): one
+        // head must fit a slot
         if (t.perm_heads > 0 &&
-            round_up(units[i] * unit_footprint(info[i], out_mask)) + 4 * kAlign > s->slot_bytes)
+            round_up((t.rows / t.perm_heads) * (t.cols / info[i].unit_values) * unit_footprint(info[i], out_mask)) +
+                    4 * kAlign > s->slot_bytes)
             return GQ_ERR_SIZE;
         bounce_in[i] = pageable(t.src);
         if (info[i].block_values == 0) {
@@ -784,7 +786,8 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
     }
 
     // Cut the work into pieces of about piece_target() bytes of slot footprint: large
-    // tensors are split on unit boundaries, small ones are packed together.
+    // tensors are split on unit boundaries (permuted ones on head boundaries), small ones
+    // are packed together.
     const size_t target = std::min(s->slot_bytes, piece_target());
     std::vector<std::vector<Member>> pieces;
     {
@@ -793,16 +796,17 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
         for (int i = 0; i < count; ++i) {
             int64_t done = 0;
             const size_t fp = unit_footprint(info[i], out_mask);
-            const size_t limit = tensors[i].perm_heads > 0 ? s->slot_bytes : target;
+            const gq_tensor_t& t = tensors[i];
+            // pieces of a permuted tensor hold whole heads
+            const int64_t step = t.perm_heads > 0 ? (t.rows / t.perm_heads) * (t.cols / info[i].unit_values) : 1;
             while (done < units[i]) {
-                const size_t room = limit > used + 4 * kAlign ? limit - used - 4 * kAlign : 0;
-                int64_t take = static_cast<int64_t>(room / fp);
-                if (tensors[i].perm_heads > 0 && take < units[i]) take = 0;
+                const size_t room = target > used + 4 * kAlign ? target - used - 4 * kAlign : 0;
+                int64_t take = static_cast<int64_t>(room / fp) / step * step;
                 if (take <= 0) {
                     if (cur.empty()) {
-                        if (limit == s->slot_bytes) return fail(GQ_ERR_SIZE);
-                        take = 1;   // one unit larger than the piece target still fits a slot
-                        if (round_up(fp) + 4 * kAlign > s->slot_bytes) return fail(GQ_ERR_SIZE);
+                        // one step larger than the piece target still fits a slot (checked above)
+                        take = step;
+                        if (round_up(step * fp) + 4 * kAlign > s->slot_bytes) return fail(GQ_ERR_SIZE);
                     } else {
                         pieces.push_back(std::move(cur));
                         cur.clear();
@@ -891,7 +895,8 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
             off = round_up(off + src_bytes);
             const bool bo = bounce_out[m.tensor];
             gq_tensor_t dt = t;
-            dt.rows = t.perm_heads > 0 ? t.rows : m.units * ti.unit_values / t.cols;
+            dt.rows = m.units * ti.unit_values / t.cols;   // whole rows for a permuted tensor
+            if (t.perm_heads > 0) dt.perm_heads = static_cast<int32_t>(dt.rows / (t.rows / t.perm_heads));
             dt.src = dsrc;
             dt.src_bytes = src_bytes;
             dt.diag = host_diags ? s->d_diag + m.tensor : nullptr;
@@ -920,7 +925,7 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
                 }
             }
             // rows of a piece: whole rows are not required (rows only matter for the
-            // permutation, which keeps tensors whole); present the piece as one row
+            // permutation, whose pieces are whole heads); present the piece as one row
             if (t.perm_heads == 0) {
                 dt.rows = 1;
                 dt.cols = nvals;

@@ -270,6 +270,50 @@ def test_unpack_gguf_tensor_non_contiguous_views(layout):
     assert same_bits(w, w2) and same_bits(s, s2)
 
 
+@pytest.mark.parametrize("heads,staging_mb", [(32, 4), (8, 12), (32, 256)])
+def test_host_path_permuted_tensor_larger_than_a_slot(heads, staging_mb):
+    """A q/k-permuted tensor larger than the session's staging slot is cut into pieces of
+    whole heads (the permutation never crosses a head): the Llama-3-8B attn_q (32 heads)
+    and attn_k shapes, codes and f32 values, against the device path."""
+    rows = 4096 if heads == 32 else 1024
+    raw = gen_tensor_bytes("Q4_K", rows * 4096, heads + staging_mb)
+    t = _run("Q4_K", raw, rows, 4096, BOTH, heads)
+    rec = N.Tensor()
+    rec.type, rec.perm_heads, rec.rows, rec.cols = FORMATS["Q4_K"].type_id, heads, rows, 4096
+    rec.src, rec.src_bytes = raw.ctypes.data, raw.size
+    codes = np.empty((rows, 4096), dtype=np.int8)
+    scales = np.empty((rows * 4096 // 32, 1), dtype=np.float32)
+    values = np.empty((rows, 4096), dtype=np.float32)
+    rec.codes, rec.scales, rec.values = codes.ctypes.data, scales.ctypes.data, values.ctypes.data
+    diag = N.Diag()
+    sess = ctypes.c_void_p()
+    N.check(N.lib().gq_session_create(0, staging_mb << 20, ctypes.byref(sess)), "gq_session_create")
+    try:
+        N.check(N.lib().gq_convert_host(sess, ctypes.byref(rec), 1, BOTH, ctypes.byref(diag)), "gq_convert_host")
+    finally:
+        N.lib().gq_session_destroy(sess)
+    assert same_bits(codes, _codes_np(t)) and same_bits(scales, t.scales.cpu().numpy())
+    assert same_bits(values, t.values.cpu().numpy())
+    r, c = diag_values(t.diag)
+    assert np.uint32(diag.round_err_bits) == np.float32(r).view(np.uint32) and diag.clip_err == int(c)
+
+
+def test_host_path_head_larger_than_a_slot_is_refused():
+    rec = N.Tensor()
+    rec.type, rec.perm_heads, rec.rows, rec.cols = FORMATS["Q4_K"].type_id, 2, 4096, 4096
+    raw = np.zeros(4096 * 16 * 144, dtype=np.uint8)
+    out = np.zeros(4096 * 4096, dtype=np.int8)
+    sc = np.zeros(4096 * 128, dtype=np.float32)
+    rec.src, rec.src_bytes, rec.codes, rec.scales = raw.ctypes.data, raw.size, out.ctypes.data, sc.ctypes.data
+    sess = ctypes.c_void_p()
+    N.check(N.lib().gq_session_create(0, 4 << 20, ctypes.byref(sess)), "gq_session_create")
+    try:
+        # one head is 2048 rows x 4096 columns: about 15 MB of slot footprint
+        assert N.lib().gq_convert_host(sess, ctypes.byref(rec), 1, N.OUT_CODES, None) == -2
+    finally:
+        N.lib().gq_session_destroy(sess)
+
+
 def test_unpack_gguf_tensor_dropin_reader(tmp_path):
     gguf = pytest.importorskip("gguf")
     from llima_b200.gguf_conversion import GgufReaderProxy
