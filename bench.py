@@ -384,61 +384,69 @@ def run_ours(args, rank, world, local_rank):
         if fmt in batches and out_mask & N.OUT_CODES:
             diag_ok &= bool((batches[fmt].diags[:, 0] != 0).any().item())
 
-    # ---- the conversion fused with the Modalix weight layout (gq_convert_modalix), one
-    # launch per tensor captured in a CUDA graph, against the two passes it replaces (the
-    # conversion above plus gq_modalix_layout on its results)
+    # ---- the conversion fused with the Modalix weight layout: every quantized tensor of
+    # this rank in one gq_convert_modalix_batch call (one launch per GGML type), against the
+    # two passes it replaces (the conversion above plus gq_modalix_layout on its results,
+    # one launch per tensor, captured in a CUDA graph)
     modalix = None
     if not args.no_modalix and out_mask == N.OUT_CODES:
         import ctypes
-        mrecs, lrecs, mbytes, malgo = [], [], 0, 0
-        for t in tensors:
+        keep, lrecs, mbytes, malgo = [], [], 0, 0
+        quant = [t for t in tensors if FORMATS[t.fmt].block_values]
+        mrecs = (N.Tensor * max(1, len(quant)))()
+        for i, t in enumerate(quant):
             f = FORMATS[t.fmt]
-            if not f.block_values:
-                continue
             oc = torch.empty((t.cols, t.rows), dtype=torch.int8, device=dev)
             os_ = torch.empty((t.cols // f.block_values, t.rows), dtype=torch.float32, device=dev)
             r = N.Tensor()
             r.type, r.perm_heads, r.rows, r.cols = f.type_id, t.perm_heads, t.rows, t.cols
             r.src, r.src_bytes, r.codes, r.scales = t.src.data_ptr(), t.src.numel(), oc.data_ptr(), os_.data_ptr()
-            mrecs.append((r, oc, os_))
+            mrecs[i] = r
+            keep.append((oc, os_))
             lrecs.append((t, oc, os_, f.block_values))
             mbytes += t.src_bytes
             malgo += piece_cost(t.fmt, t.rows, t.cols, "codes")
-        # launches go to the current stream (the capture stream while a graph is recorded)
+        n_types = len({t.fmt for t in quant})
+
         def mstep():
             sid = torch.cuda.current_stream().cuda_stream
-            for r, _, _ in mrecs:
-                N.check(N.lib().gq_convert_modalix(ctypes.byref(r), r.rows, sid), "gq_convert_modalix")
+            N.check(N.lib().gq_convert_modalix_batch(mrecs, None, len(quant), sid), "gq_convert_modalix_batch")
 
+        # launches go to the current stream (the capture stream while a graph is recorded)
         def lstep():
             sid = torch.cuda.current_stream().cuda_stream
             for t, oc, os_, blk in lrecs:
                 N.check(N.lib().gq_modalix_layout(t.codes.data_ptr(), t.scales.data_ptr(), t.rows, t.cols, blk, t.rows,
                                                   oc.data_ptr(), os_.data_ptr(), sid), "gq_modalix_layout")
 
-        def graph_ms(fn, n):
+        def events_ms(fn, n, graph=False):
             for _ in range(3):
                 fn()
             torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                fn()
-            g.replay()
+            g = None
+            if graph:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    fn()
+                run = g.replay
+            else:
+                run = fn
+            run()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(n):
-                g.replay()
+                run()
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / n
             del g
             return ms
 
-        if mrecs:
+        if quant:
             barrier()
-            m_ms = graph_ms(mstep, 20)
-            l_ms = graph_ms(lstep, 20)
+            m_ms = events_ms(mstep, 20)
+            l_ms = events_ms(lstep, 20, graph=True)
             agg = torch.tensor([m_ms, l_ms], dtype=torch.float64, device=dev)
             tot = torch.tensor([float(mbytes), float(malgo)], dtype=torch.float64, device=dev)
             if world > 1:
@@ -450,8 +458,8 @@ def run_ours(args, rank, world, local_rank):
                        "ms_per_model": round(m_ms, 4),
                        "hbm_frac": round(float(tot[1].item()) / (m_ms / 1e3) / 1e9 / (peak_ * world), 4),
                        "two_pass_ms_per_model": round(ms_step + l_ms, 4), "layout_pass_ms": round(l_ms, 4),
-                       "launches_per_step": len(mrecs), "api": "gq_convert_modalix (CUDA graph of per-tensor launches)"}
-        del mrecs, lrecs
+                       "launches_per_step": n_types, "api": "gq_convert_modalix_batch (one launch per GGML type)"}
+        del mrecs, lrecs, keep
 
     # ---- token-embedding rows for the runtime (gq_embedding_rows: force_float dequantize,
     # x embed_scale, bf16 round, per-row int8 with a bf16 scale), on this rank's piece of

@@ -26,7 +26,7 @@
  *   gq_requantize_symmetric         sima_lmm/gguf/ggml_quant.py:785-886 (requantize_symmetric)
  *   gq_query                        sizes implied by ggml_quant.py:104-131 (format table)
  *   gq_convert_host                 the same as gq_convert_batch, on host buffers
- *   gq_convert_modalix              unpack_gguf_tensor followed by ModelGraph._build_conv's
+ *   gq_convert_modalix(_batch)      unpack_gguf_tensor followed by ModelGraph._build_conv's
  *                                   layout (sima_lmm/model/model_graph.py:1012-1079), fused
  *   gq_unpack_fields                sima_lmm/gguf/ggml_quant.py:567-694 (unpack_k_quant) and
  *                                   :174-271 (unpack_q4 / unpack_q5, ASYMMETRIC)
@@ -171,6 +171,12 @@ GQ_API int gq_modalix_layout(const void* codes, const float* scales, int64_t row
  * other shapes return GQ_ERR_SIZE (convert, then gq_modalix_layout).  Device pointers:
  * src 16-byte aligned, scales 4. */
 GQ_API int gq_convert_modalix(const gq_tensor_t* tensor, int64_t rows_padded, void* stream);
+
+/* gq_convert_modalix for `count` tensors with one launch per GGML type present (at most 128
+ * tensors per launch); rows_padded[i] per tensor, or NULL for no padding.  Each tensor's
+ * diag, if any, is zeroed first. */
+GQ_API int gq_convert_modalix_batch(const gq_tensor_t* tensors, const int64_t* rows_padded, int32_t count,
+                                    void* stream);
 
 /* The field-level steps of the reference's ggml_quant module, for callers that use them
  * one by one (the conversion entry points above fuse them).

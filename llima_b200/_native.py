@@ -23,7 +23,7 @@ EXPORTS = ("gq_version", "gq_strerror", "gq_last_cuda_error", "gq_query", "gq_di
            "gq_convert", "gq_convert_batch", "gq_requantize_symmetric", "gq_session_create",
            "gq_session_destroy", "gq_convert_host", "gq_convert_host_noalloc", "gq_embedding_rows",
            "gq_quantize_rows", "gq_modalix_layout", "gq_unpack_fields", "gq_remove_superblocks",
-           "gq_convert_modalix")
+           "gq_convert_modalix", "gq_convert_modalix_batch")
 
 
 class NativeLibraryError(RuntimeError):
@@ -86,6 +86,7 @@ def _declare(lib):
         "gq_modalix_layout": ([P, P, I64, I64, I32, I64, P, P, P], ctypes.c_int),
         "gq_unpack_fields": ([I32, P, SZ, I64, P, P, P, P], ctypes.c_int),
         "gq_convert_modalix": ([ctypes.POINTER(Tensor), I64, P], ctypes.c_int),
+        "gq_convert_modalix_batch": ([ctypes.POINTER(Tensor), P, I32, P], ctypes.c_int),
         "gq_remove_superblocks": ([P, P, I32, I64, I32, I32, P, P, P], ctypes.c_int),
     }
     for name, (args, res) in sig.items():

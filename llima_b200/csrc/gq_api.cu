@@ -254,9 +254,13 @@ int gq_requantize_symmetric(const float* block_consts, const int8_t* codes, int6
                                           out_codes, diag, stream));
 }
 
-int gq_convert_modalix(const gq_tensor_t* tensor, int64_t rows_padded, void* stream) {
-    if (tensor == nullptr) return GQ_ERR_NULL;
-    const gq_tensor_t& t = *tensor;
+}  // extern "C"
+
+namespace {
+
+// Checks of one tensor for the fused layout writer and its descriptor (tile_begin 0).
+// Returns GQ_OK with *empty set when there is nothing to launch.
+int modalix_desc(const gq_tensor_t& t, int64_t rows_padded, gq::GqModalix* m, bool* empty) {
     TypeInfo ti;
     int64_t nv = 0, nu = 0;
     const int st = shape_check(t, &ti, &nv, &nu);
@@ -267,32 +271,88 @@ int gq_convert_modalix(const gq_tensor_t* tensor, int64_t rows_padded, void* str
     if (t.cols % gq::kModalixCols != 0) return GQ_ERR_SIZE;
     const int64_t upr = t.cols / ti.unit_values;
     if ((upr * ti.unit_bytes) % 16 != 0) return GQ_ERR_SIZE;
-    if (t.cols == 0 || rows_padded == 0) return GQ_OK;
+    *empty = t.cols == 0 || rows_padded == 0;
+    if (*empty) return GQ_OK;
     if (t.codes == nullptr || t.scales == nullptr) return GQ_ERR_NULL;
     if (t.rows > 0 && t.src == nullptr) return GQ_ERR_NULL;
     if (!aligned(t.src, 16) || !aligned(t.scales, 4)) return GQ_ERR_ALIGN;
-    if (t.diag != nullptr) {
-        if (!aligned(t.diag, 4)) return GQ_ERR_ALIGN;
-        const int e = gq_diag_reset(t.diag, 1, stream);
-        if (e != GQ_OK) return e;
-    }
-    gq::GqModalix m{};
-    m.src = static_cast<const uint8_t*>(t.src);
-    m.out_codes = static_cast<uint8_t*>(t.codes);
-    m.out_scales = t.scales;
-    m.diag = (ti.asym && t.diag != nullptr) ? t.diag : nullptr;
-    m.rows = t.rows;
-    m.cols = t.cols;
-    m.rows_padded = rows_padded;
-    m.units_per_row = upr;
+    if (t.diag != nullptr && !aligned(t.diag, 4)) return GQ_ERR_ALIGN;
     const int64_t n_col = t.cols / gq::kModalixCols;
     const int64_t n_tiles = (rows_padded + gq::kModalixRows - 1) / gq::kModalixRows * n_col;
     if (n_tiles >= (int64_t(1) << 31)) return GQ_ERR_SIZE;
-    m.n_col_tiles = static_cast<uint32_t>(n_col);
-    m.n_tiles = static_cast<uint32_t>(n_tiles);
-    gq::fast_div_params(m.n_col_tiles, m.ncol_mul, m.ncol_shift);
-    m.head_dim = t.perm_heads > 0 ? static_cast<int32_t>(t.rows / t.perm_heads) : 0;
-    return cuda_status(gq::launch_modalix(t.type, m, stream));
+    *m = gq::GqModalix{};
+    m->src = static_cast<const uint8_t*>(t.src);
+    m->out_codes = static_cast<uint8_t*>(t.codes);
+    m->out_scales = t.scales;
+    m->diag = (ti.asym && t.diag != nullptr) ? t.diag : nullptr;
+    m->rows = t.rows;
+    m->cols = t.cols;
+    m->rows_padded = rows_padded;
+    m->units_per_row = upr;
+    m->n_col_tiles = static_cast<uint32_t>(n_col);
+    m->n_tiles = static_cast<uint32_t>(n_tiles);
+    gq::fast_div_params(m->n_col_tiles, m->ncol_mul, m->ncol_shift);
+    m->head_dim = t.perm_heads > 0 ? static_cast<int32_t>(t.rows / t.perm_heads) : 0;
+    return GQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gq_convert_modalix_batch(const gq_tensor_t* tensors, const int64_t* rows_padded, int32_t count,
+                             void* stream) {
+    if (count < 0) return GQ_ERR_ARG;
+    if (count > 0 && tensors == nullptr) return GQ_ERR_NULL;
+    std::vector<std::pair<gq::GqModalix, int>> items;
+    items.reserve(count);
+    for (int i = 0; i < count; ++i) {
+        const gq_tensor_t& t = tensors[i];
+        gq::GqModalix m;
+        bool empty = false;
+        const int st = modalix_desc(t, rows_padded ? rows_padded[i] : t.rows, &m, &empty);
+        if (st != GQ_OK) return st;
+        if (t.diag != nullptr) {
+            const int e = gq_diag_reset(t.diag, 1, stream);
+            if (e != GQ_OK) return e;
+        }
+        if (!empty) items.emplace_back(m, t.type);
+    }
+    static const int kTypes[] = {GQ_TYPE_Q4_K, GQ_TYPE_Q6_K, GQ_TYPE_Q5_K, GQ_TYPE_Q8_0, GQ_TYPE_Q4_0,
+                                 GQ_TYPE_Q4_1, GQ_TYPE_Q5_0, GQ_TYPE_Q5_1, GQ_TYPE_Q2_K, GQ_TYPE_Q3_K};
+    std::unique_ptr<gq::GqModalixBatch> b(new (std::nothrow) gq::GqModalixBatch);
+    if (!b) return GQ_ERR_NOMEM;
+    for (int type : kTypes) {
+        b->n = 0;
+        b->total_tiles = 0;
+        for (size_t i = 0; i <= items.size(); ++i) {
+            const bool last = i == items.size();
+            if (!last && items[i].second == type) {
+                if (static_cast<uint64_t>(b->total_tiles) + items[i].first.n_tiles >= (uint64_t(1) << 31)) {
+                    const int e = cuda_status(gq::launch_modalix(type, *b, stream));
+                    if (e != GQ_OK) return e;
+                    b->n = 0;
+                    b->total_tiles = 0;
+                }
+                gq::GqModalix m = items[i].first;
+                m.tile_begin = b->total_tiles;
+                b->total_tiles += m.n_tiles;
+                b->d[b->n++] = m;
+            }
+            if ((last || b->n == gq::kMaxModalix) && b->n > 0) {
+                const int e = cuda_status(gq::launch_modalix(type, *b, stream));
+                if (e != GQ_OK) return e;
+                b->n = 0;
+                b->total_tiles = 0;
+            }
+        }
+    }
+    return GQ_OK;
+}
+
+int gq_convert_modalix(const gq_tensor_t* tensor, int64_t rows_padded, void* stream) {
+    if (tensor == nullptr) return GQ_ERR_NULL;
+    return gq_convert_modalix_batch(tensor, &rows_padded, 1, stream);
 }
 
 int gq_unpack_fields(int32_t type, const void* src, size_t src_bytes, int64_t n_units, float* super_consts,

@@ -62,13 +62,21 @@ struct GqModalix {
     uint32_t n_col_tiles, n_tiles;
     uint32_t ncol_mul, ncol_shift;   // division by n_col_tiles (fast_div_params)
     int32_t head_dim;         // > 0: llama q/k head permutation with heads of this size
-    int32_t pad;
+    uint32_t tile_begin;      // first tile of this tensor in its batch
+};
+
+// Tensors of one GGML type converted into the Modalix layout by one launch.
+constexpr int kMaxModalix = 128;
+struct GqModalixBatch {
+    int32_t n;
+    uint32_t total_tiles;
+    GqModalix d[kMaxModalix];
 };
 
 // launch entry points implemented in gq_kernels.cu
 int launch_batch(int type, int out_mask, const GqBatch& batch, void* stream);
 int64_t tiles_for(int type, int64_t n_units);
-int launch_modalix(int type, const GqModalix& m, void* stream);
+int launch_modalix(int type, const GqModalixBatch& b, void* stream);
 constexpr int kModalixRows = 128;   // output channels per tile of the fused layout writer
 constexpr int kModalixCols = 256;   // input channels per tile
 int launch_layout(const uint8_t* codes, const float* scales, int64_t rows, int64_t cols, int64_t nb,

@@ -922,7 +922,7 @@ __device__ __forceinline__ uint32_t modalix_src_row(const GqModalix& m, uint32_t
 }
 
 template <int TYPE>
-__global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constant__ GqModalix m) {
+__global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constant__ GqModalixBatch b) {
     using X = MxFmt<TYPE>;
     constexpr int MODE = kOutCodes | kOutSmem;
     extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -940,12 +940,22 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
     const int warp = threadIdx.x >> 5;
     uint8_t* staging = smem + X::kTBytes + X::kRBytes + X::kSBytes + warp * X::kWarpStaging;
     __syncthreads();
-    const uint32_t ncol = m.n_col_tiles, rows = static_cast<uint32_t>(m.rows);
 
-    // tile t: row block rb (output channels d0..d0+127), column block cb (256 input channels)
+    // a CTA visits its tiles in increasing order, so each tensor cursor only moves forward
+    int c_issue = 0, c_tile = 0;
+    auto seek = [&](int& c, uint32_t t) -> const GqModalix& {
+        while (c + 1 < b.n && b.d[c + 1].tile_begin <= t) ++c;
+        return b.d[c];
+    };
+
+    // tile t of the batch: tensor m, row block rb (output channels d0..d0+127), column
+    // block cb (256 input channels)
     auto issue = [&](uint32_t t) {
-        if (t >= m.n_tiles) return;
-        const uint32_t rb = fast_div(t, m.ncol_mul, m.ncol_shift), cb = t - rb * ncol;
+        if (t >= b.total_tiles) return;
+        const GqModalix& m = seek(c_issue, t);
+        const uint32_t lt = t - m.tile_begin;
+        const uint32_t rb = fast_div(lt, m.ncol_mul, m.ncol_shift), cb = lt - rb * m.n_col_tiles;
+        const uint32_t rows = static_cast<uint32_t>(m.rows);
         const uint32_t o_lane = rb * kModalixRows + 16 * warp + (lane & 15);
         // lanes 0..15: byte offset of row (lane)'s segment, or -1 past the last row
         int64_t seg = -1;
@@ -965,16 +975,18 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
     };
 
     DiagAcc acc;
-    acc.target = m.diag;
     GqDesc dt{};
     dt.codes = rtile;
     dt.scales = stile;
-    dt.diag = m.diag;
 
     uint32_t t = blockIdx.x;
     issue(t);
-    for (; t < m.n_tiles; t += gridDim.x) {
-        const uint32_t rb = fast_div(t, m.ncol_mul, m.ncol_shift), cb = t - rb * ncol;
+    for (; t < b.total_tiles; t += gridDim.x) {
+        const GqModalix& m = seek(c_tile, t);
+        acc.retarget(m.diag, lane);
+        const uint32_t lt = t - m.tile_begin;
+        const uint32_t rb = fast_div(lt, m.ncol_mul, m.ncol_shift), cb = lt - rb * m.n_col_tiles;
+        const uint32_t rows = static_cast<uint32_t>(m.rows);
         const uint32_t d0 = rb * kModalixRows;
         // rows of this tile below `rows` (0..128)
         const int valid_rows = d0 >= rows ? 0 : (rows - d0 < kModalixRows ? static_cast<int>(rows - d0) : kModalixRows);
@@ -1175,7 +1187,7 @@ int64_t tiles_for(int type, int64_t n_units) {
 namespace {
 
 template <int TYPE>
-int launch_modalix_t(const GqModalix& m, cudaStream_t s) {
+int launch_modalix_t(const GqModalixBatch& m, cudaStream_t s) {
     using X = MxFmt<TYPE>;
     static_assert(X::kSmem <= 113 * 1024, "two CTAs per SM");
     static int per_sm[64] = {0};
@@ -1189,7 +1201,7 @@ int launch_modalix_t(const GqModalix& m, cudaStream_t s) {
             occ = 1;
     }
     const int64_t cap = static_cast<int64_t>(device_info().sms) * occ;
-    const int blocks = static_cast<int>(m.n_tiles < cap ? m.n_tiles : cap);
+    const int blocks = static_cast<int>(m.total_tiles < cap ? m.total_tiles : cap);
     if (blocks <= 0) return 0;
     gq_modalix_kernel<TYPE><<<blocks, 256, X::kSmem, s>>>(m);
     return static_cast<int>(cudaGetLastError());
@@ -1197,7 +1209,7 @@ int launch_modalix_t(const GqModalix& m, cudaStream_t s) {
 
 }  // namespace
 
-int launch_modalix(int type, const GqModalix& m, void* stream) {
+int launch_modalix(int type, const GqModalixBatch& m, void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (type) {
         case GQ_TYPE_Q4_K: return launch_modalix_t<GQ_TYPE_Q4_K>(m, s);
