@@ -249,16 +249,45 @@ __device__ __forceinline__ void quantize_row_blocks(const uint8_t* row, int64_t 
         float A, B;
         decode_block<TYPE>(row, b, w, A, B);
         uint32_t c[8];
+        if (fast) {
+            // two values per instruction (f32x2: each half an IEEE round-to-nearest op, the
+            // same results as the scalar chain), the bf16 rounding of a pair in one cvt
+            const float2 A2 = make_float2(A, A), nB2 = make_float2(-B, -B);
+            const float2 s2 = make_float2(embed_scale, embed_scale), rs2 = make_float2(rs, rs);
 #pragma unroll
-        for (int i = 0; i < E::NW; ++i) {
-            uint32_t packed = 0;
+            for (int i = 0; i < E::NW; ++i) {
+                uint32_t packed = 0;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int q = static_cast<int>((w[i] >> (8 * e)) & 0xFFu) - E::OFF;
-                const float y = to_bf16(__fmul_rn(block_value<TYPE>(A, B, q), embed_scale));
-                packed |= (static_cast<uint32_t>(row_code(y, step, rs, fast)) & 0xFFu) << (8 * e);
+                for (int e = 0; e < 4; e += 2) {
+                    const float2 q2 = make_float2(static_cast<float>(static_cast<int>((w[i] >> (8 * e)) & 0xFFu) - E::OFF),
+                                                  static_cast<float>(static_cast<int>((w[i] >> (8 * e + 8)) & 0xFFu) - E::OFF));
+                    float2 x2 = __fmul2_rn(A2, q2);
+                    if constexpr (E::kSub) x2 = __fadd2_rn(x2, nB2);
+                    const float2 y2 = __bfloat1622float2(__float22bfloat162_rn(__fmul2_rn(x2, s2)));
+                    const float2 t2 = __fmul2_rn(y2, rs2);
+                    float kx = rintf(t2.x), ky = rintf(t2.y);
+                    const float2 d2 = __fadd2_rn(t2, make_float2(-kx, -ky));
+                    // within 2^-12 of a half-integer: the exactly divided quotient decides
+                    if (fabsf(fabsf(d2.x) - 0.5f) < 2.44140625e-4f) kx = rintf(__fdiv_rn(y2.x, step));
+                    if (fabsf(fabsf(d2.y) - 0.5f) < 2.44140625e-4f) ky = rintf(__fdiv_rn(y2.y, step));
+                    const int cx = min(max(__float2int_rn(kx), -127), 127);
+                    const int cy = min(max(__float2int_rn(ky), -127), 127);
+                    packed |= ((static_cast<uint32_t>(cx) & 0xFFu) | ((static_cast<uint32_t>(cy) & 0xFFu) << 8)) << (8 * e);
+                }
+                c[i] = packed;
             }
-            c[i] = packed;
+        } else {
+#pragma unroll
+            for (int i = 0; i < E::NW; ++i) {
+                uint32_t packed = 0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int q = static_cast<int>((w[i] >> (8 * e)) & 0xFFu) - E::OFF;
+                    const float y = to_bf16(__fmul_rn(block_value<TYPE>(A, B, q), embed_scale));
+                    packed |= (static_cast<uint32_t>(row_code(y, step, rs, fast)) & 0xFFu) << (8 * e);
+                }
+                c[i] = packed;
+            }
         }
         int8_t* dst = out + b * E::BV;
         if (vec) {
