@@ -282,6 +282,58 @@ def workload_config(args, world) -> dict:
             "l2": "inputs larger than L2 (GGUF bytes >> 126 MB), no flush"}
 
 
+def gguf_file_e2e(tensors, host_src, layers: int = 8):
+    """GB/s of convert_gguf_file on a real GGUF file: the embedding, the output head and
+    the first `layers` layers of the rank's tensors written with gguf-py's writer to a
+    scratch file (page-cached; /dev/shm when it has room), converted once to warm the page
+    cache and the session, then timed once.  None when there is no room for the file."""
+    import shutil
+    import numpy as np
+    import gguf
+    from llima_b200.gguf_conversion import convert_gguf_file
+    keep = [(t, hs) for t, hs in zip(tensors, host_src)
+            if not t.name.startswith("blk.") or int(t.name.split(".")[1]) < layers]
+    total = sum(hs.numel() for _, hs in keep)
+    d = "/dev/shm" if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > 3 * total \
+        else tempfile.gettempdir()
+    if shutil.disk_usage(d).free < 3 * total:
+        return None
+    path = os.path.join(d, f"llima_b200_bench_{os.getpid()}.gguf")
+    try:
+        w = gguf.GGUFWriter(path, "llama")
+        heads = {t.name.split(".")[-2]: t.perm_heads for t, _ in keep if t.perm_heads}
+        w.add_block_count(layers)
+        if "attn_q" in heads:
+            w.add_head_count(heads["attn_q"])
+            w.add_head_count_kv(heads.get("attn_k", heads["attn_q"]))
+        for t, hs in keep:
+            raw = hs.numpy()
+            if t.fmt == "F32":
+                w.add_tensor(t.name, raw.view(np.float32).reshape(t.rows) if t.cols == 1
+                             else raw.view(np.float32).reshape(t.rows, t.cols))
+            else:
+                w.add_tensor(t.name, raw.reshape(t.rows, -1), raw_shape=(t.rows, raw.size // t.rows),
+                             raw_dtype=getattr(gguf.GGMLQuantizationType, t.fmt))
+        w.write_header_to_file()
+        w.write_kv_data_to_file()
+        w.write_tensors_to_file()
+        w.close()
+        del w
+        res = convert_gguf_file(path)
+        del res
+        t0 = time.perf_counter()
+        res = convert_gguf_file(path)
+        dt = time.perf_counter() - t0
+        n = len(res)
+        del res
+        return {"value": round(total / dt / 1e9, 3), "unit": "GB/s", "seconds": round(dt, 4), "gguf_bytes": total,
+                "tensors": n, "cut": f"embedding, output and the first {layers} layers",
+                "api": "convert_gguf_file (GGUFReader memory map, one gq_convert_host call)"}
+    finally:
+        if os.path.exists(path):
+            os.unlink(path)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -563,6 +615,8 @@ def run_ours(args, rank, world, local_rank):
         barrier()
         dropin_bytes = float(sum(r.size for _, r in quant))
         del quant
+        # from a GGUF file on one GPU (ranks of a multi-GPU run would each need their own)
+        file_e2e = gguf_file_e2e(tensors, host_src) if world == 1 else None
         h2d = sum(h.numel() for h in host_src)
         d2h = sum(ht.numel() * ht.element_size() for outs in host_out for ht in outs.values())
         agg = torch.tensor([float(gguf_bytes), float(h2d), float(d2h), 1.0 if same else 0.0, dropin_bytes],
@@ -577,7 +631,8 @@ def run_ours(args, rank, world, local_rank):
                "dropin_pageable": {"value": round(float(agg[4].item()) / float(tmax.item()) / 1e9, 3), "unit": "GB/s",
                                    "s_per_model": round(float(tmax.item()), 4),
                                    "api": "gguf_conversion.convert_host, one call per tensor, pageable numpy "
-                                          "in/out (GgufModel.load_weight's path)"}}
+                                          "in/out (GgufModel.load_weight's path)"},
+               "from_gguf_file": file_e2e}
         del host_src, host_out
 
     tot = torch.tensor([float(gguf_bytes), float(out_bytes), 1.0 if diag_ok else 0.0], dtype=torch.float64,

@@ -29,8 +29,8 @@ from ml_dtypes import bfloat16, int4
 from . import _native as N
 from .formats import FORMAT_BY_ID, FORMATS
 
-__all__ = ["unpack_gguf_tensor", "load_tensor", "load_partition", "convert_host", "GgufReaderProxy",
-           "install", "requant_warning"]
+__all__ = ["unpack_gguf_tensor", "load_tensor", "load_partition", "convert_host", "convert_gguf_file",
+           "GgufReaderProxy", "install", "requant_warning"]
 
 # Same logger and text as ggml_quant.py:879-880, so log handling stays as it was.
 _log = logging.getLogger("sima_lmm.gguf.ggml_quant")
@@ -138,6 +138,98 @@ def convert_host(fmt: str, raw: np.ndarray, rows: int, cols: int, force_float: b
     if fmt == "Q4_0":
         codes = codes.view(np.uint8).view(int4)
     return scales, codes, d
+
+
+def convert_gguf_file(path, names=None, force_float: bool = False, permute_qk: bool | None = None,
+                      device: int | None = None, reader=None) -> dict:
+    """Every quantized tensor of a GGUF file (or the ``names`` given) in one host-buffer
+    call, so that the copies, the kernels and the result copies of all tensors overlap:
+    ``{name: (scales | None, weights)}`` with the values ``unpack_gguf_tensor`` returns for
+    each tensor (float tensors are passed through on the host as it does).
+
+    ``permute_qk``: apply the llama / mistral q/k head permutation to ``attn_q`` / ``attn_k``
+    weights and biases as ``GgufModel.load_weight`` does (``gguf_conversion.py:285-332``);
+    ``None`` decides from the file's ``general.architecture`` (``llama``).  The
+    requantization warning is logged per tensor, as the reference logs it per call."""
+    if reader is None:
+        from gguf import GGUFReader
+        reader = GGUFReader(path)
+    fields = reader.fields
+
+    def field(key):
+        f = fields.get(key)
+        if f is None:
+            return None
+        v = f.contents()
+        if isinstance(v, (list, np.ndarray)):
+            return int(np.max(v))
+        return v
+
+    arch = field("general.architecture")
+    if permute_qk is None:
+        permute_qk = arch == "llama"
+    n_head = field(f"{arch}.attention.head_count") if arch else None
+    n_kv = field(f"{arch}.attention.head_count_kv") if arch else None
+    wanted = None if names is None else set(names)
+    out: dict = {}
+    jobs = []
+    for t in reader.tensors:
+        if wanted is not None and t.name not in wanted:
+            continue
+        heads = 0
+        if permute_qk and n_head:
+            if t.name.endswith(("attn_q.weight", "attn_q.bias")):
+                heads = int(n_head)
+            elif t.name.endswith(("attn_k.weight", "attn_k.bias")):
+                heads = int(n_kv or n_head)
+        fmt = _type_name(t.tensor_type)
+        if fmt in ("F32", "F16", "BF16"):
+            out[t.name] = load_tensor(t, force_float, heads)
+            continue
+        if fmt == "Q8_1" and not force_float:
+            raise KeyError("Q8_1")
+        if fmt not in _GPU_TYPES:
+            raise NotImplementedError(f"GGML type {fmt} is not handled by the B200 GGUF path")
+        jobs.append((t, fmt, heads))
+    if not jobs:
+        return out
+    recs = (N.Tensor * len(jobs))()
+    diags = (N.Diag * len(jobs))()
+    results = []
+    for i, (t, fmt, heads) in enumerate(jobs):
+        f = FORMATS[fmt]
+        shape = tuple(int(x) for x in t.shape[::-1])
+        rows = shape[0]
+        cols = int(np.prod(shape[1:])) if len(shape) > 1 else 1
+        if f.asymmetric and not force_float and rows * cols == 0:
+            raise ValueError("zero-size array to reduction operation maximum which has no identity")
+        raw = np.ascontiguousarray(np.asarray(t.data)).reshape(-1).view(np.uint8)
+        r = N.Tensor()
+        r.type, r.perm_heads, r.rows, r.cols = f.type_id, heads, rows, cols
+        r.src, r.src_bytes = _host_ptr(raw), raw.size
+        if force_float:
+            values = _host_empty((rows, cols), np.float32)
+            r.values = _host_ptr(values)
+            results.append((t.name, fmt, shape, raw, None, values))
+        else:
+            codes = _host_empty((rows, cols), np.int8)
+            scales = _host_empty((rows * cols // f.block_values, 1), np.float32)
+            r.codes, r.scales = _host_ptr(codes), _host_ptr(scales)
+            results.append((t.name, fmt, shape, raw, scales, codes))
+        recs[i] = r
+    dev = _device() if device is None else device
+    mask = N.OUT_F32 if force_float else N.OUT_CODES
+    N.check(N.lib().gq_convert_host(_session(dev), recs, len(jobs), mask, diags), "gq_convert_host")
+    for (name, fmt, shape, _raw, scales, w), dg in zip(results, diags):
+        if force_float:
+            out[name] = (None, w.reshape(shape))
+            continue
+        if FORMATS[fmt].asymmetric:
+            requant_warning(np.array([dg.round_err_bits], dtype=np.uint32).view(np.float32)[0], np.int16(dg.clip_err))
+        if fmt == "Q4_0":
+            w = w.view(np.uint8).view(int4)
+        out[name] = (scales, w.reshape(shape))
+    return out
 
 
 def _type_name(tensor_type) -> str:

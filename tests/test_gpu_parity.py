@@ -314,6 +314,52 @@ def test_host_path_head_larger_than_a_slot_is_refused():
         N.lib().gq_session_destroy(sess)
 
 
+def test_convert_gguf_file_matches_per_tensor_decode(tmp_path):
+    """convert_gguf_file: every tensor of a llama GGUF file in one host call, with the q/k
+    permutation taken from the file's architecture and head counts, equal to the oracle's
+    unpack (+ _permute_qk_proj) of each tensor; a subset by name; force_float."""
+    gguf = pytest.importorskip("gguf")
+    from llima_b200.gguf_conversion import convert_gguf_file
+    path = tmp_path / "m.gguf"
+    w = gguf.GGUFWriter(str(path), "llama")
+    w.add_block_count(1)
+    w.add_head_count(8)
+    w.add_head_count_kv(2)
+    specs = {"token_embd.weight": ("Q6_K", 96, 512), "blk.0.attn_q.weight": ("Q4_K", 512, 512),
+             "blk.0.attn_k.weight": ("Q5_K", 128, 512), "blk.0.attn_v.weight": ("Q8_0", 128, 512),
+             "blk.0.ffn_up.weight": ("Q4_0", 300, 512), "blk.0.ffn_down.weight": ("Q2_K", 512, 768)}
+    raws = {}
+    for i, (name, (fmt, r, c)) in enumerate(specs.items()):
+        raw = gen_tensor_bytes(fmt, r * c, 60 + i)
+        w.add_tensor(name, raw.reshape(r, -1), raw_shape=(r, raw.size // r),
+                     raw_dtype=getattr(gguf.GGMLQuantizationType, fmt))
+        raws[name] = raw
+    norm = np.random.default_rng(2).normal(1, 0.02, 512).astype(np.float32)
+    w.add_tensor("blk.0.attn_norm.weight", norm)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    got = convert_gguf_file(path)
+    assert set(got) == set(specs) | {"blk.0.attn_norm.weight"}
+    heads = {"blk.0.attn_q.weight": 8, "blk.0.attn_k.weight": 2}
+    for name, (fmt, r, c) in specs.items():
+        with np.errstate(all="ignore"):
+            s2, q2, _ = O.unpack_tensor(fmt, raws[name].tobytes(), (r, c), log=False)
+        if name in heads:
+            s2, q2 = O.permute_qk(s2, q2, heads[name])
+        s, q = got[name]
+        assert q.dtype == q2.dtype and q.shape == (r, c), name
+        assert same_bits(q.view(np.uint8), q2.view(np.uint8)) and same_bits(s, s2), name
+    assert got["blk.0.attn_norm.weight"][0] is None
+    assert np.array_equal(got["blk.0.attn_norm.weight"][1], norm)
+    sub = convert_gguf_file(path, names=["blk.0.attn_v.weight"], permute_qk=False)
+    assert list(sub) == ["blk.0.attn_v.weight"]
+    ff = convert_gguf_file(path, names=["blk.0.ffn_down.weight"], force_float=True)
+    want = O.gguf_dequantize(raws["blk.0.ffn_down.weight"].tobytes(), "Q2_K").reshape(512, 768)
+    assert ff["blk.0.ffn_down.weight"][0] is None and same_bits(ff["blk.0.ffn_down.weight"][1], want)
+
+
 def test_unpack_gguf_tensor_dropin_reader(tmp_path):
     gguf = pytest.importorskip("gguf")
     from llima_b200.gguf_conversion import GgufReaderProxy
