@@ -821,8 +821,20 @@ __global__ void __launch_bounds__(kThreads) gq_copy_kernel(const __grid_constant
         const uint8_t* src = D.src + b0;
         uint8_t* dst = reinterpret_cast<uint8_t*>(D.values) + b0;
         if (D.perm_heads == 0) {
-            for (int c = lane * 16; c + 16 <= nbytes; c += 32 * 16)
-                stg128(dst + c, __ldg(reinterpret_cast<const uint4*>(src + c)));
+            // all of the lane's loads go out before its stores (one memory latency per
+            // tile instead of one per 512 bytes)
+            constexpr int kRounds = kCopyTileBytes / (32 * 16);
+            uint4 v[kRounds];
+#pragma unroll
+            for (int k = 0; k < kRounds; ++k) {
+                const int c = lane * 16 + k * 32 * 16;
+                if (c + 16 <= nbytes) v[k] = __ldg(reinterpret_cast<const uint4*>(src + c));
+            }
+#pragma unroll
+            for (int k = 0; k < kRounds; ++k) {
+                const int c = lane * 16 + k * 32 * 16;
+                if (c + 16 <= nbytes) stg128(dst + c, v[k]);
+            }
             for (int c = (nbytes & ~15) + lane * ES; c < nbytes; c += 32 * ES) {
                 if (ES == 4) *reinterpret_cast<uint32_t*>(dst + c) = *reinterpret_cast<const uint32_t*>(src + c);
                 else *reinterpret_cast<uint16_t*>(dst + c) = *reinterpret_cast<const uint16_t*>(src + c);
