@@ -186,38 +186,65 @@ struct FastRequant {
     float scale;      // S / sf
     float round_err;  // |rm - r * sf| (good blocks), else 0
     float r;          // M / S' (exact when `finite`)
-    float sf0;        // min(16, lo_out/lo, hi_out/hi) before the integer rounding (exact when `finite`)
+    float sf0;        // min(16, lo_out/lo, hi_out/hi) before the integer rounding: exact
+                      // when > 0.98 and S, M are finite; a smaller one is exact_sf0(den)
+    float den;        // the denominator of that quotient (lo or hi), 0 when neither bound applies
     bool good;
     bool finite;      // S and M are finite
 };
 
-__device__ __forceinline__ FastRequant requant_fast(float S, float M, int qmin, int qmax, int lo_out, int hi_out,
-                                                    const float* recip) {
+// rcp.approx of -b: the negation goes into the approximation's operand.
+__device__ __forceinline__ float rcp_approx_neg(float b) {
+    float y;
+    asm("{ .reg .f32 t; neg.f32 t, %1; rcp.approx.f32 %0, t; }" : "=f"(y) : "f"(b));
+    return y;
+}
+
+// The requantization parameters of one block (lo_out = -128, hi_out = 127): S is the
+// block scale, P = -M the block min before its negation.  This is requant_block's fast
+// case with two divisions replaced: r = RN(M / S') by quotient_f16 (S' = M when S = 0 and
+// |M| > eps gives r = 1 exactly), and the bound quotient
+// sf0 = min(16, -128/lo, 127/hi) by Markstein's division with a refined reciprocal
+// (P. Markstein, IBM J. Res. Dev. 34(1), 1990), whose floor and comparison with 0.98
+// equal those of the IEEE quotient for every reachable denominator (exhaustive check:
+// tests/numerics/scale_factor_quotient.c), so sfi, rm, good and scale are requant_block's.
+// A block whose sf0 is at most 0.98 takes the rare path, which recomputes the quotient
+// from `den` with an IEEE division (exact_sf0).
+__device__ __forceinline__ FastRequant requant_fast(float S, float P, int qmin, int qmax, const float* recip) {
     FastRequant p;
-    const float s_eff = (S == 0.0f) ? ((fabsf(M) > kScaleEpsilon) ? M : kScaleEpsilon) : S;
-    const float r = quotient_f16(M, s_eff);
+    const bool zero = S == 0.0f;
+    const float s = zero ? kScaleEpsilon : S;
+    const float r = (zero && fabsf(P) > kScaleEpsilon) ? 1.0f : quotient_f16(P, -s);   // RN(M / s)
     const float lo = __fadd_rn(static_cast<float>(qmin), r);
     const float hi = __fadd_rn(static_cast<float>(qmax), r);
-    // sf = min(16, lo_out/lo, hi_out/hi) as in requant_block (the smaller quotient found
-    // with one exact fma); both operands of the division are positive multiples here
-    const bool need_lo = lo < static_cast<float>(lo_out) / 16.0f;
-    const bool need_hi = hi > static_cast<float>(hi_out) / 16.0f;
-    const float e = __fmaf_rn(-static_cast<float>(hi_out), lo, __fmul_rn(static_cast<float>(lo_out), hi));
-    const bool use_lo = need_lo && (!need_hi || e > 0.0f);
-    const float t = __fdiv_rn(static_cast<float>(use_lo ? lo_out : hi_out), use_lo ? lo : hi);
-    const float sf0 = (need_lo || need_hi) ? fminf(16.0f, t) : 16.0f;   // in (0, 16] or NaN
-    const bool big = sf0 > 0.98f;
-    const float sf = fmaxf(floorf(sf0), 1.0f);                          // 1..16 (NaN -> 1)
+    const bool need_lo = lo < -8.0f;
+    const bool need_hi = hi > 127.0f / 16.0f;
+    // which bound sets sf (see requant_block): -128*hi - 127*lo > 0 <=> -128/lo < 127/hi
+    const float w = __fmaf_rn(-127.0f, lo, __fmul_rn(-128.0f, hi));
+    const bool use_lo = need_lo && (!need_hi || w > 0.0f);
+    const float num = use_lo ? -128.0f : 127.0f;
+    const float den = use_lo ? lo : hi;
+    // t = num / den with nz = -z, z ~ 1/den: e2 = 1 + den*nz, nz1 = -(z refined once),
+    // nq0 = -RN(num * z1), rem = num - den*q0 (exact), t = -nq1 = q0 + rem*z1
+    const float nz = rcp_approx_neg(den);
+    const float ez = __fmaf_rn(den, nz, 1.0f);
+    const float nz1 = __fmaf_rn(ez, nz, nz);
+    const float nq0 = __fmul_rn(num, nz1);
+    const float rem = __fmaf_rn(den, nq0, num);
+    const float nt = __fmaf_rn(rem, nz1, nq0);
+    const float sf0 = (need_lo || need_hi) ? fminf(16.0f, -nt) : 16.0f;
+    const float sf = fmaxf(floorf(sf0), 1.0f);
     p.sfi = static_cast<int>(sf);
     const float rmv = __fmul_rn(r, sf);
     p.rm = __float2int_rn(rmv);
     // for big blocks |r * sf| < 2200 (see requant_block), so these sums do not wrap
     const int vmin = qmin * p.sfi + p.rm, vmax = qmax * p.sfi + p.rm;
-    const bool finite = fabsf(S) < __int_as_float(0x7f800000) && fabsf(M) < __int_as_float(0x7f800000);
-    p.good = finite && big && vmin >= lo_out && vmax <= hi_out;
-    p.finite = finite;
+    const float inf = __int_as_float(0x7f800000);
+    p.finite = fabsf(S) < inf && fabsf(P) < inf;
+    p.good = p.finite && sf0 > 0.98f && vmin >= -128 && vmax <= 127;
     p.r = r;
     p.sf0 = sf0;
+    p.den = (need_lo || need_hi) ? den : 0.0f;
     p.round_err = p.good ? fabsf(__fsub_rn(rintf(rmv), rmv)) : 0.0f;
     // S / sf for an integer sf and finite S: q0 = S*(1/sf) and one fma correction, exact
     // for every f16-derived S (tests/numerics/div_by_small_int.c)
@@ -228,9 +255,15 @@ __device__ __forceinline__ FastRequant requant_fast(float S, float M, int qmin, 
     return p;
 }
 
+// The exact sf0 of a block whose bound quotient came out at most 0.98 in requant_fast
+// (num / den by IEEE division), 16 when no bound applies (den == 0).
+__device__ __forceinline__ float exact_sf0(float den) {
+    return den == 0.0f ? 16.0f : fminf(16.0f, __fdiv_rn(den < 0.0f ? -128.0f : 127.0f, den));
+}
+
 // Finish one block whose S and M are finite but that is not `good` (non-integer scale
 // factor or clipping), one value per lane of the warp, from requant_fast's exact r and
-// sf0 (ggml_quant.py:859-882): sf, rm and the block scale as requant_block derives them,
+// exact sf0 (ggml_quant.py:859-882): sf, rm and the block scale as requant_block derives them,
 // the per-value codes and the clipping error as the largest |clip(v) - v| of the block.
 // Returns the block's rounding and clipping errors (the same in every lane).
 template <int MODE = kOutCodes>

@@ -333,13 +333,13 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
         const int qminH = min(aminH & 0xFFFF, aminH >> 16), qmaxH = max(amaxH & 0xFFFF, amaxH >> 16);
 
         // block constants f16(f32 product), min negated (ggml_quant.py:771-777), then
-        // requantize_symmetric (ggml_quant.py:785-886) for the common case
+        // requantize_symmetric (ggml_quant.py:785-886) for the common case (P = -M)
         const float SL = round_to_f16(__fmul_rn(static_cast<float>(scL), d));
         const float SH = round_to_f16(__fmul_rn(static_cast<float>(scH), d));
-        const float ML = -round_to_f16(__fmul_rn(static_cast<float>(mnL), dmin));
-        const float MH = -round_to_f16(__fmul_rn(static_cast<float>(mnH), dmin));
-        const FastRequant pL = requant_fast(SL, ML, qminL, qmaxL, -128, 127, recip);
-        const FastRequant pH = requant_fast(SH, MH, qminH, qmaxH, -128, 127, recip);
+        const float PL = round_to_f16(__fmul_rn(static_cast<float>(mnL), dmin));
+        const float PH = round_to_f16(__fmul_rn(static_cast<float>(mnH), dmin));
+        const FastRequant pL = requant_fast(SL, PL, qminL, qmaxL, recip);
+        const FastRequant pH = requant_fast(SH, PH, qminH, qmaxH, recip);
         if (valid) {
             st_out<MODE>(reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g), make_float2(pL.scale, pH.scale));
             acc.add(fmaxf(pL.round_err, pH.round_err), 0);
@@ -398,7 +398,9 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
                 } else {
                     const float bS = __shfl_sync(kFull, side ? SH : SL, src);
                     const float br = __shfl_sync(kFull, side ? pH.r : pL.r, src);
-                    const float bsf0 = __shfl_sync(kFull, side ? pH.sf0 : pL.sf0, src);
+                    float bsf0 = __shfl_sync(kFull, side ? pH.sf0 : pL.sf0, src);
+                    const float bden = __shfl_sync(kFull, side ? pH.den : pL.den, src);
+                    if (!(bsf0 > 0.98f)) bsf0 = exact_sf0(bden);
                     e = finish_block<MODE>(side ? qhi : qlo, bS, br, bsf0, -128, 127, D.codes + soff + 32 * side + lane,
                                      D.scales + (soff >> 5) + side, lane);
                 }

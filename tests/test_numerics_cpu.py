@@ -46,3 +46,21 @@ def test_invariant_divisor_parameters(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0, out.stdout
     assert "mismatches 0" in out.stdout
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_scale_factor_quotient_keeps_floor_and_threshold(tmp_path):
+    # gq_device.cuh's requant_fast finds sf0 = min(16, -128/lo, 127/hi) by Markstein's
+    # division from a reciprocal approximation; this checks, for every denominator the fast
+    # path can reach and every reciprocal within 2 ulp, that its floor and its comparison
+    # with 0.98 equal the IEEE quotient's (the rare path recomputes the quotient itself).
+    exe = tmp_path / "scale_factor_quotient"
+    cmd = ["gcc", "-O2", "-ffp-contract=off", "-o", str(exe),
+           str(HERE / "numerics" / "scale_factor_quotient.c"), "-lm"]
+    if subprocess.run(["gcc", "-fopenmp", "-x", "c", "-", "-o", str(tmp_path / "omp")], input="int main(){return 0;}",
+                      capture_output=True, text=True).returncode == 0:
+        cmd.insert(1, "-fopenmp")
+    subprocess.run(cmd, check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout
+    assert out.stdout.count("violations 0") == 2
