@@ -161,20 +161,6 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     return p;
 }
 
-// RN(a / b) for f32 values a, b that are widened finite f16 values (b != 0), without a
-// branch.  y = rcp.approx(b) is within 1 ulp of 1/b; e = 1 - b*y is exact in one fma (b
-// has at most 11 significant bits); y + e*y approximates 1/b to about 2^-45 relative, and
-// a*(y + e*y) rounded once is RN(a/b), since a quotient of two 11-bit significands lies at
-// least 2^-36 (relative) from every f32 rounding midpoint.  Checked exhaustively, with any
-// y within 2 ulp, by tests/numerics/f16_quotient.c.  A zero quotient may come out with
-// either sign (no caller distinguishes them).
-__device__ __forceinline__ float quotient_f16(float a, float b) {
-    float y;
-    asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(b));
-    const float e = __fmaf_rn(-b, y, 1.0f);
-    return __fmaf_rn(a, y, __fmul_rn(a, __fmul_rn(e, y)));
-}
-
 // The common case of requant_block on its own: finite S and M, an integer scale factor
 // (sf > 0.98) and no code that clips.  Such a block is `good` and its fields equal
 // requant_block's; for any other block `good` is false, round_err is 0 and the other
@@ -202,8 +188,8 @@ __device__ __forceinline__ float rcp_approx_neg(float b) {
 
 // The requantization parameters of one block (lo_out = -128, hi_out = 127): S is the
 // block scale, P = -M the block min before its negation.  This is requant_block's fast
-// case with two divisions replaced: r = RN(M / S') by quotient_f16 (S' = M when S = 0 and
-// |M| > eps gives r = 1 exactly), and the bound quotient
+// case with two divisions replaced: r = RN(M / S') from a reciprocal approximation (S' = M
+// when S = 0 and |M| > eps gives r = 1 exactly), and the bound quotient
 // sf0 = min(16, -128/lo, 127/hi) by Markstein's division with a refined reciprocal
 // (P. Markstein, IBM J. Res. Dev. 34(1), 1990), whose floor and comparison with 0.98
 // equal those of the IEEE quotient for every reachable denominator (exhaustive check:
@@ -214,7 +200,17 @@ __device__ __forceinline__ FastRequant requant_fast(float S, float P, int qmin, 
     FastRequant p;
     const bool zero = S == 0.0f;
     const float s = zero ? kScaleEpsilon : S;
-    const float r = (zero && fabsf(P) > kScaleEpsilon) ? 1.0f : quotient_f16(P, -s);   // RN(M / s)
+    // r = RN(M / s) = RN(P / -s), both operands widened finite f16 values, without a
+    // branch: with b = -s and y = rcp.approx(b) (within 1 ulp of 1/b), e = 1 - b*y is exact
+    // in one fma (b has at most 11 significant bits); y + e*y approximates 1/b to about
+    // 2^-45 relative, and P*(y + e*y) rounded once is RN(P/b), since a quotient of two
+    // 11-bit significands lies at least 2^-36 (relative) from every f32 rounding midpoint.
+    // Checked exhaustively, with any y within 2 ulp, by tests/numerics/f16_quotient.c.  A
+    // zero quotient may come out with either sign (nothing below distinguishes them).
+    const float ny = rcp_approx_neg(s);
+    const float e = __fmaf_rn(s, ny, 1.0f);
+    const float rq = __fmaf_rn(P, ny, __fmul_rn(P, __fmul_rn(e, ny)));
+    const float r = (zero && fabsf(P) > kScaleEpsilon) ? 1.0f : rq;
     const float lo = __fadd_rn(static_cast<float>(qmin), r);
     const float hi = __fadd_rn(static_cast<float>(qmax), r);
     const bool need_lo = lo < -8.0f;
