@@ -80,7 +80,8 @@ def test_format_table_matches_oracle():
 
 
 def test_model_sets_match_baseline_totals():
-    # SURVEY/BASELINE totals: 291 / 339 / 723 tensors, 5.308 / 5.646 / 45.25 GB of GGUF bytes
+    # the Llama-3-8B, Qwen2.5-7B and Llama-3-70B benchmark sets: 291 / 339 / 723 tensors,
+    # 5.308 / 5.646 / 45.25 GB of GGUF bytes
     want = {"llama3-8b": (291, 5_307_858_944), "qwen2.5-7b": (339, 5_645_588_480),
             "llama3-70b": (723, 45_250_183_168)}
     for m, (n, nb) in want.items():
