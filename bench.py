@@ -52,6 +52,11 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0,
                     help="keep only the first L transformer layers (small cases for profiling)")
     ap.add_argument("--formats", default="", help="comma list of GGML formats to keep (profiling)")
+    ap.add_argument("--no-sustained", action="store_true", help="skip the >= 1 s steady-state timing")
+    ap.add_argument("--sustained-seconds", type=float, default=1.5)
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the BASELINE config sub-records (C1 Q8_0, C2 Q4_0 / Q4_K, C4 Qwen2.5-7B set)")
+    ap.add_argument("--no-70b", action="store_true", help="skip the Llama-3-70B set sub-record")
     return ap.parse_args()
 
 
@@ -219,7 +224,8 @@ class ClockSampler:
         self.proc.wait()
         self.file.flush()
         self.file.seek(0)
-        sm, mx, reasons = [], [], set()
+        sm, mx, pw, reasons = [], [], [], set()
+        capped = 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.file.read().splitlines():
             parts = [p.strip() for p in line.split(",")]
@@ -230,14 +236,20 @@ class ClockSampler:
                 mx.append(float(parts[2]))
             except ValueError:
                 continue
+            try:
+                pw.append(float(parts[3]))
+            except ValueError:
+                pass
             for n, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
+                    capped += n == "sw_power_cap"
         os.unlink(self.file.name)
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
-                "reasons": sorted(reasons)}
+                "reasons": sorted(reasons), "sw_power_cap_share": round(capped / len(sm), 3),
+                "power_w_median": statistics.median(pw) if pw else None}
 
 
 def measured_peak():
@@ -334,59 +346,51 @@ def gguf_file_e2e(tensors, host_src, layers: int = 8):
             os.unlink(path)
 
 
-def run_ours(args, rank, world, local_rank):
-    import torch
-    import torch.distributed as dist
+class DeviceSet:
+    """One rank's shard of a tensor set resident in HBM: the GGUF bytes of its pieces (byte-
+    balanced over the ranks, no exchange), their outputs, and one DeviceBatch per GGML type
+    (one launch each per step)."""
+    ORDER = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "F32"]
 
-    from llima_b200 import _native as N
-    from llima_b200.device import DeviceBatch, DeviceTensor, alloc_outputs
-    from llima_b200.formats import FORMATS
-    from llima_b200.shard import piece_cost, plan_shards
-    from llima_b200.synth import gen_tensor_bytes_torch, head_count_for
+    def __init__(self, specs, model, rank, world, dev, out_mask, out_name):
+        import torch
+        from llima_b200.device import DeviceBatch, DeviceTensor, alloc_outputs
+        from llima_b200.formats import FORMATS
+        from llima_b200.shard import piece_cost, plan_shards
+        from llima_b200.synth import gen_tensor_bytes_torch, head_count_for
+        plan = plan_shards([(s.fmt, s.rows, s.cols, head_count_for(model, s.name) > 0) for s in specs],
+                           world, out_name)
+        by_index: dict[int, list] = {}
+        for pc in plan[rank]:
+            by_index.setdefault(pc.index, []).append(pc)
+        self.tensors = []
+        for idx, plist in by_index.items():
+            sp = specs[idx]
+            full = gen_tensor_bytes_torch(sp.fmt, sp.n_values, sp.seed, dev, sp.kind)
+            f = FORMATS[sp.fmt]
+            row_bytes = sp.cols // f.unit_values * f.unit_bytes
+            for pc in plist:
+                src = full[pc.row0 * row_bytes:pc.row1 * row_bytes].clone()
+                heads = head_count_for(model, sp.name) if pc.rows == sp.rows else 0
+                t = DeviceTensor(sp.fmt, pc.rows, sp.cols, src, heads, name=sp.name)
+                self.tensors.append(alloc_outputs(t, out_mask))
+            del full
+        torch.cuda.synchronize()
+        self.batches = {}
+        for fmt in self.ORDER:
+            ts = [t for t in self.tensors if t.fmt == fmt]
+            if ts:
+                self.batches[fmt] = DeviceBatch(ts, out_mask)
+        self.algo = {fmt: sum(piece_cost(fmt, t.rows, t.cols, out_name) for t in b.tensors)
+                     for fmt, b in self.batches.items()}
+        self.gguf_bytes = sum(t.src_bytes for t in self.tensors)
+        self.out_bytes = sum(t.out_bytes for t in self.tensors)
+        self.launches_per_step = sum(-(-len(b.tensors) // 256) for b in self.batches.values())
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    out_mask = {"codes": N.OUT_CODES, "f32": N.OUT_F32, "both": N.OUT_CODES | N.OUT_F32}[args.out]
-    N.lib()   # fail loudly before any work if the library is missing
-
-    specs = selected_specs(args)
-    plan = plan_shards([(s.fmt, s.rows, s.cols, head_count_for(args.model, s.name) > 0) for s in specs],
-                       world, args.out)
-    mine = plan[rank]
-    tensors: list[DeviceTensor] = []
-    by_index: dict[int, list] = {}
-    for p in mine:
-        by_index.setdefault(p.index, []).append(p)
-    for idx, plist in by_index.items():
-        s = specs[idx]
-        full = gen_tensor_bytes_torch(s.fmt, s.n_values, s.seed, dev, s.kind)
-        f = FORMATS[s.fmt]
-        row_bytes = s.cols // f.unit_values * f.unit_bytes
-        for p in plist:
-            src = full[p.row0 * row_bytes:p.row1 * row_bytes].clone()
-            heads = head_count_for(args.model, s.name) if p.rows == s.rows else 0
-            t = DeviceTensor(s.fmt, p.rows, s.cols, src, heads, name=s.name)
-            tensors.append(alloc_outputs(t, out_mask))
-        del full
-    torch.cuda.synchronize()
-
-    order = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "F32"]
-    batches = {}
-    for fmt in order:
-        ts = [t for t in tensors if t.fmt == fmt]
-        if ts:
-            batches[fmt] = DeviceBatch(ts, out_mask)
-    algo = {fmt: sum(piece_cost(fmt, t.rows, t.cols, args.out) for t in b.tensors) for fmt, b in batches.items()}
-    gguf_bytes = sum(t.src_bytes for t in tensors)
-    out_bytes = sum(t.out_bytes for t in tensors)
-    launches_per_step = sum(-(-len(b.tensors) // 256) for b in batches.values())
-
-    stream = torch.cuda.current_stream()
-    ev = {fmt: [] for fmt in batches}
-
-    def step(record: bool):
-        for fmt, b in batches.items():
-            if record:
+    def step(self, stream, ev=None):
+        import torch
+        for fmt, b in self.batches.items():
+            if ev is not None:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
@@ -396,38 +400,194 @@ def run_ours(args, rank, world, local_rank):
             else:
                 b.run(stream, reset_diag=False)
 
+    def reset_diag(self, stream):
+        for b in self.batches.values():
+            b.run(stream, reset_diag=True)
+
+    def free(self):
+        import torch
+        self.tensors = []
+        self.batches = {}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+
+def rank_max(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def rank_sum(xs: list, world: int, dev) -> list:
+    if world == 1:
+        return [float(x) for x in xs]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x) for x in xs], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return [float(v) for v in t.tolist()]
+
+
+def rank_gather(x: float, world: int, dev) -> list:
+    """x of every rank, in rank order."""
+    if world == 1:
+        return [float(x)]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], dtype=torch.float64, device=dev)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
+def timed_steps(ds: DeviceSet, steps: int, warmup: int, world: int, dev, sampler=None, per_format=True):
+    """Whole steps of `ds` timed with CUDA events on the launching stream between barriers
+    and synchronizes; returns the max-over-ranks ms per step, this rank's per-format kernel
+    ms per launch, every rank's kernel time per step (work_ms) and the clock record."""
+    import torch
+    import torch.distributed as dist
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+    for _ in range(warmup):
+        ds.step(stream)
+    torch.cuda.synchronize()
+    barrier()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ev = {fmt: [] for fmt in ds.batches} if per_format else None
+    torch.cuda.synchronize()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        ds.step(stream, ev)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms_step = rank_max(t0.elapsed_time(t1), world, dev) / steps
+    per_fmt = {fmt: sum(a.elapsed_time(b) for a, b in lst) / len(lst) for fmt, lst in ev.items()} if ev else {}
+    work = rank_gather(sum(per_fmt.values()), world, dev) if ev else None
+    return ms_step, per_fmt, work, clocks
+
+
+def work_record(work: list | None) -> dict | None:
+    if not work:
+        return None
+    return {"per_rank": [round(w, 4) for w in work], "max": round(max(work), 4), "min": round(min(work), 4),
+            "unit": "ms of kernel time per step (sum of the rank's per-format launch events)"}
+
+
+
+def single_tensor_rate(fmt: str, rows: int, cols: int, dev, world: int, peak: float) -> dict:
+    """One tensor per launch, as BASELINE's single-tensor configs give it.  Copies of the
+    tensor (different seeds) rotate so that consecutive launches read more than L2 holds;
+    one launch per copy is captured in a CUDA graph (a host call per launch would take
+    longer than the kernel) and the graph is replayed, timed with CUDA events.  With N
+    ranks every rank converts its own copies (replicas); the slowest rank is reported."""
+    import torch
+    import torch.distributed as dist
+    from llima_b200 import _native as N
+    from llima_b200.device import DeviceBatch, DeviceTensor, alloc_outputs
+    from llima_b200.formats import FORMATS
+    from llima_b200.shard import piece_cost
+    from llima_b200.synth import gen_tensor_bytes_torch
+    cost = piece_cost(fmt, rows, cols, "codes")
+    n_copies = max(2, -(-3 * (126 << 20) // cost))
+    copies = []
+    for i in range(n_copies):
+        src = gen_tensor_bytes_torch(fmt, rows * cols, 7000 + i, dev)
+        copies.append(DeviceBatch([alloc_outputs(DeviceTensor(fmt, rows, cols, src), N.OUT_CODES)], N.OUT_CODES))
+    stream = torch.cuda.current_stream()
+    for b in copies:
+        b.run(stream, reset_diag=True)
+    for _ in range(3):
+        for b in copies:
+            b.run(stream, reset_diag=False)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for b in copies:
+            b.run(reset_diag=False)
+    g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    reps = max(5, -(-2000 // n_copies))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = rank_max(e0.elapsed_time(e1), world, dev) / (reps * n_copies)
+    del g
+    f = FORMATS[fmt]
+    gguf = rows * cols // f.unit_values * f.unit_bytes
+    out = {"shape": [rows, cols], "format": fmt, "ms_per_launch": round(ms, 5),
+           "value": round(gguf / (ms / 1e3) / 1e9, 1), "unit": "GB/s of GGUF",
+           "hbm_frac": round(cost / (ms / 1e3) / 1e9 / peak, 4), "algorithmic_bytes": cost,
+           "kernel": f"gq_convert_kernel<{fmt}>", "launches_timed": reps * n_copies,
+           "copies": n_copies, "l2": "rotating copies, more than 3x L2 between reuses"}
+    del copies
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from llima_b200 import _native as N
+    from llima_b200.formats import FORMATS
+    from llima_b200.shard import piece_cost
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    out_mask = {"codes": N.OUT_CODES, "f32": N.OUT_F32, "both": N.OUT_CODES | N.OUT_F32}[args.out]
+    N.lib()   # fail loudly before any work if the library is missing
+
+    specs = selected_specs(args)
+    ds = DeviceSet(specs, args.model, rank, world, dev, out_mask, args.out)
+    tensors = ds.tensors
+    batches = ds.batches
+    algo = ds.algo
+    gguf_bytes = ds.gguf_bytes
+    out_bytes = ds.out_bytes
+    launches_per_step = ds.launches_per_step
+    stream = torch.cuda.current_stream()
+
     def barrier():
         if world > 1:
             dist.barrier()
 
-    for b in batches.values():
-        b.run(stream, reset_diag=True)
-    for _ in range(args.warmup):
-        step(False)
-    torch.cuda.synchronize()
-    barrier()
+    ds.reset_diag(stream)
     sampler = ClockSampler([local_rank] if world == 1 else list(range(world))) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
-    torch.cuda.synchronize()
-    barrier()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for _ in range(args.steps):
-        step(True)
-    t_end.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    clocks = sampler.stop() if sampler else None
-    ms_total = t_start.elapsed_time(t_end)
-    per_fmt_ms = {fmt: sum(a.elapsed_time(b) for a, b in lst) / len(lst) for fmt, lst in ev.items()}
-    if world > 1:
-        t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = float(t.item())
-    ms_step = ms_total / args.steps
+    ms_step, per_fmt_ms, work, clocks = timed_steps(ds, args.steps, args.warmup, world, dev, sampler)
+
+    # ---- the same step held for >= --sustained-seconds: the board's power cap engages
+    # after a fraction of a second, so this is the rate a long conversion job runs at
+    sustained = None
+    if not args.no_sustained:
+        n_sus = max(args.steps, int(args.sustained_seconds * 1e3 / max(ms_step, 1e-3)) + 1)
+        sam = ClockSampler([local_rank] if world == 1 else list(range(world))) if rank == 0 else None
+        ms_sus, _, _, clk_sus = timed_steps(ds, n_sus, 3, world, dev, sam, per_format=False)
+        peak_, _ = measured_peak()
+        tot_s = rank_sum([gguf_bytes, out_bytes], world, dev)
+        sustained = {"value": round(tot_s[0] / (ms_sus / 1e3) / 1e9, 2), "unit": "GB/s", "steps": n_sus,
+                     "seconds": round(n_sus * ms_sus / 1e3, 3), "ms_per_step": round(ms_sus, 4),
+                     "hbm_frac_whole_step": round((tot_s[0] + tot_s[1]) / (ms_sus / 1e3) / 1e9 / (peak_ * world), 4),
+                     "clocks": clk_sus}
 
     # correctness guard on the timed buffers: the diagnostics of the asymmetric formats
     # must have been written (rounding error of random data is > 0)
@@ -635,6 +795,50 @@ def run_ours(args, rank, world, local_rank):
                "from_gguf_file": file_e2e}
         del host_src, host_out
 
+    # ---- the other BASELINE workloads, each after the previous one's memory is freed
+    del tensors, batches
+    ds.free()
+    full_set = not (args.layers or args.formats) and out_mask == N.OUT_CODES
+    peak_, _ = measured_peak()
+    configs = None
+    if not args.no_configs and full_set:
+        from llima_b200.synth import model_specs
+        configs = {}
+        for key, fmt, rows, cols in (("C1_Q8_0_4096x4096", "Q8_0", 4096, 4096),
+                                     ("C2_Q4_0_11008x4096", "Q4_0", 11008, 4096),
+                                     ("C2_Q4_K_11008x4096", "Q4_K", 11008, 4096)):
+            configs[key] = single_tensor_rate(fmt, rows, cols, dev, world, peak_)
+        if args.model != "qwen2.5-7b":
+            qs = DeviceSet(model_specs("qwen2.5-7b", args.seed), "qwen2.5-7b", rank, world, dev, out_mask, "codes")
+            qs.reset_diag(stream)
+            ms_q, per_q, work_q, _ = timed_steps(qs, max(5, min(args.steps, 20)), 3, world, dev)
+            tot_q = rank_sum([qs.gguf_bytes, qs.out_bytes], world, dev)
+            configs["C4_qwen2.5-7b_set"] = {
+                "value": round(tot_q[0] / (ms_q / 1e3) / 1e9, 2), "unit": "GB/s of GGUF",
+                "ms_per_model": round(ms_q, 4),
+                "hbm_frac": round((tot_q[0] + tot_q[1]) / (ms_q / 1e3) / 1e9 / (peak_ * world), 4),
+                "gguf_bytes": int(tot_q[0]), "out_bytes": int(tot_q[1]), "work_ms": work_record(work_q),
+                "per_format_GBps": {k: round(qs.algo[k] / (v / 1e3) / 1e9, 1) for k, v in per_q.items()},
+                "per_format_frac": {k: round(qs.algo[k] / (v / 1e3) / 1e9 / peak_, 4) for k, v in per_q.items()}}
+            qs.free()
+    llama3_70b = None
+    if not args.no_70b and full_set and args.model != "llama3-70b":
+        from llima_b200.synth import model_specs
+        ds70 = DeviceSet(model_specs("llama3-70b", args.seed), "llama3-70b", rank, world, dev, out_mask, "codes")
+        ds70.reset_diag(stream)
+        sam70 = ClockSampler([local_rank] if world == 1 else list(range(world))) if rank == 0 else None
+        n70 = max(3, min(args.steps, 10))
+        ms70, per70, work70, clk70 = timed_steps(ds70, n70, 2, world, dev, sam70)
+        tot70 = rank_sum([ds70.gguf_bytes, ds70.out_bytes], world, dev)
+        llama3_70b = {
+            "s_per_model": round(ms70 / 1e3, 6), "value": round(tot70[0] / (ms70 / 1e3) / 1e9, 2),
+            "unit": "GB/s of GGUF", "n_gpus": world, "steps": n70,
+            "hbm_frac": round((tot70[0] + tot70[1]) / (ms70 / 1e3) / 1e9 / (peak_ * world), 4),
+            "gguf_bytes": int(tot70[0]), "out_bytes": int(tot70[1]), "work_ms": work_record(work70),
+            "per_format_GBps_rank0": {k: round(ds70.algo[k] / (v / 1e3) / 1e9, 1) for k, v in per70.items()},
+            "clocks": clk70, "sharding": "tensors and row ranges byte-balanced over the ranks, no collective"}
+        ds70.free()
+
     tot = torch.tensor([float(gguf_bytes), float(out_bytes), 1.0 if diag_ok else 0.0], dtype=torch.float64,
                        device=dev)
     if world > 1:
@@ -662,7 +866,9 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded, BASELINE distributions)",
         "config": workload_config(args, world),
         "roofline": roofline, "gpu_launches": launches_per_step * args.steps, "diag_written": bool(tot[2].item() == world),
+        "work_ms": work_record(work), "sustained": sustained,
         "e2e": e2e, "clocks": clocks, "modalix_fused": modalix, "embedding_rows": embedding,
+        "configs": configs, "llama3_70b": llama3_70b,
     }
     return line
 

@@ -229,7 +229,8 @@ GQ_API int gq_quantize_rows(const float* x, int64_t rows, int64_t cols, int8_t* 
  * (copied directly) or pageable (bounced through the pinned slots).  The pointers in
  * `tensors` are HOST pointers; diags (optional, host, one per tensor) receive the maxima.
  * Calls on one session are serialized.  A session belongs to the process that created it
- * (a forked child creates its own). */
+ * (a forked child creates its own).  The caller's current device is the same after each
+ * of these calls as before it. */
 typedef struct gq_session gq_session_t;
 GQ_API int gq_session_create(int32_t device, size_t staging_bytes, gq_session_t** out);
 GQ_API int gq_session_destroy(gq_session_t* session);
@@ -247,7 +248,15 @@ GQ_API int gq_convert_host(gq_session_t* session, const gq_tensor_t* tensors, in
  * (NULL = legacy default stream), one piece at a time, and the call returns when the
  * results are in host memory.
  *   - The first call on a device looks up the array's device address (with `device`
- *     made current); make that first call before any stream capture.
+ *     made current); make that first call before any stream capture.  The array's
+ *     device memory is committed when the library's device code is loaded on that
+ *     device, which under CUDA's lazy module loading (the default since CUDA 12.2) is
+ *     this first call: a caller that hands all of a device's memory to another
+ *     allocator should first make one call with count = 0 on that device (it loads the
+ *     code, reserves the array and converts nothing).  A failed load is GQ_ERR_CUDA.
+ *   - The caller's current device is the same after the call as before it.
+ *   - An error after work was queued returns only once that work has finished, so no
+ *     copy lands in the caller's buffers afterwards; the outputs are then incomplete.
  *   - Limits: the first 64 KiB of the array hold the diagnostics, so at most 8192 tensors
  *     per call when host_diags is given; the rest stages one piece at a time, so a piece
  *     of one unit (a head of rows for a permuted tensor) must fit.  Larger requests fail

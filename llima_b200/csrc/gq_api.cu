@@ -691,13 +691,29 @@ struct Member {
     int64_t units;
 };
 
-int guard_device(int device) {
-    int cur = -1;
-    cudaError_t e = cudaGetDevice(&cur);
-    if (e != cudaSuccess) return cuda_status(e);
-    if (cur != device) return cuda_status(cudaSetDevice(device));
-    return GQ_OK;
-}
+// Makes `device` current for one entry-point call and puts the caller's current device
+// back on every return path (hosts such as torch keep their own notion of it).
+class DeviceScope {
+public:
+    explicit DeviceScope(int device) {
+        status_ = cuda_status(cudaGetDevice(&prev_));
+        if (status_ == GQ_OK && prev_ != device) {
+            status_ = cuda_status(cudaSetDevice(device));
+            switched_ = status_ == GQ_OK;
+        }
+    }
+    ~DeviceScope() {
+        if (switched_) cudaSetDevice(prev_);
+    }
+    DeviceScope(const DeviceScope&) = delete;
+    DeviceScope& operator=(const DeviceScope&) = delete;
+    int status() const { return status_; }
+
+private:
+    int prev_ = 0;
+    int status_ = GQ_OK;
+    bool switched_ = false;
+};
 
 // Pinned bounce slots and the copy pool, on the first request with a pageable buffer.
 // Without them (pinned allocation refused) pageable buffers are handed to the copy
@@ -728,8 +744,8 @@ int gq_session_create(int32_t device, size_t staging_bytes, gq_session_t** out) 
     if (out == nullptr) return GQ_ERR_NULL;
     *out = nullptr;
     if (staging_bytes < (1u << 20)) return GQ_ERR_ARG;
-    int st = guard_device(device);
-    if (st != GQ_OK) return st;
+    const DeviceScope scope(device);
+    if (scope.status() != GQ_OK) return scope.status();
     std::unique_ptr<gq_session> s(new (std::nothrow) gq_session);
     if (!s) return GQ_ERR_NOMEM;
     s->device = device;
@@ -753,7 +769,7 @@ int gq_session_create(int32_t device, size_t staging_bytes, gq_session_t** out) 
 
 int gq_session_destroy(gq_session_t* s) {
     if (s == nullptr) return GQ_OK;
-    cudaSetDevice(s->device);
+    const DeviceScope scope(s->device);
     for (int i = 0; i < kSlots; ++i) {
         if (s->stream[i]) cudaStreamSynchronize(s->stream[i]);
     }
@@ -777,7 +793,8 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
     if (count > 0 && tensors == nullptr) return GQ_ERR_NULL;
     if (!valid_mask(out_mask)) return GQ_ERR_ARG;
     std::lock_guard<std::mutex> session_lock(s->mu);
-    int st = guard_device(s->device);
+    const DeviceScope scope(s->device);
+    int st = scope.status();
     if (st != GQ_OK) return st;
 
     std::vector<TypeInfo> info(count);
@@ -1106,18 +1123,33 @@ int gq_convert_host_noalloc(int32_t device, const gq_tensor_t* tensors, int32_t 
         const int64_t min_units = t.perm_heads > 0 ? (t.rows / t.perm_heads) * upr : 1;
         if (static_cast<size_t>(min_units) * fp + 4 * kAlign > staging) return GQ_ERR_SIZE;
     }
-    int st = guard_device(device);
+    // the lock is taken before the device scope, so the caller's device is restored first
+    // and the mutex is released last, after any queued work has drained
+    std::lock_guard<std::mutex> lock(g_noalloc[device].mu);
+    const DeviceScope scope(device);
+    int st = scope.status();
     if (st != GQ_OK) return st;
     NoAllocDevice* nd = nullptr;
-    std::lock_guard<std::mutex> lock(g_noalloc[device].mu);
     if ((st = noalloc_setup(device, &nd)) != GQ_OK) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     gq_diag_t* d_diag = reinterpret_cast<gq_diag_t*>(nd->scratch);
     uint8_t* base = nd->scratch + kNoAllocDiagBytes;
+    // Once anything is queued, an error return first waits for the stream (its status is
+    // not what the caller needs: the first error is), so that no copy still lands in the
+    // caller's buffers and no queued work still uses the array after the call returns.
+    bool queued = false;
+    auto fail = [&](int e) {
+        if (queued) {
+            cudaStreamSynchronize(s);
+            cudaGetLastError();
+        }
+        return e;
+    };
     if (host_diags != nullptr && count > 0) {
         // the array keeps the previous call's contents: the maxima must start at zero
         st = cuda_status(cudaMemsetAsync(d_diag, 0, sizeof(gq_diag_t) * count, s));
-        if (st != GQ_OK) return st;
+        if (st != GQ_OK) return fail(st);
+        queued = true;
     }
     gq::GqBatch& b = nd->batch;
     for (int i = 0; i < count; ++i) {
@@ -1150,7 +1182,8 @@ int gq_convert_host_noalloc(int32_t device, const gq_tensor_t* tensors, int32_t 
             dt.diag = host_diags ? d_diag + i : nullptr;
             st = cuda_status(cudaMemcpyAsync(base, static_cast<const uint8_t*>(t.src) + u0 * ti.unit_bytes,
                                              dt.src_bytes, cudaMemcpyHostToDevice, s));
-            if (st != GQ_OK) return st;
+            if (st != GQ_OK) return fail(st);
+            queued = true;
             void* h_dst[3] = {nullptr, nullptr, nullptr};
             const void* d_src[3] = {nullptr, nullptr, nullptr};
             size_t n_bytes[3] = {0, 0, 0};
@@ -1185,11 +1218,11 @@ int gq_convert_host_noalloc(int32_t device, const gq_tensor_t* tensors, int32_t 
             b.d[0] = make_desc(dt, ti, n);
             b.d[0].tile_begin = 0;
             const int e = gq::launch_batch(t.type, out_mask, b, s);
-            if (e != 0) return cuda_status(e);
+            if (e != 0) return fail(cuda_status(e));
             for (int k = 0; k < 3; ++k) {
                 if (n_bytes[k] == 0) continue;
                 st = cuda_status(cudaMemcpyAsync(h_dst[k], d_src[k], n_bytes[k], cudaMemcpyDeviceToHost, s));
-                if (st != GQ_OK) return st;
+                if (st != GQ_OK) return fail(st);
             }
             // the next piece overwrites the staging bytes: stream order puts its copy
             // after these reads
@@ -1197,7 +1230,7 @@ int gq_convert_host_noalloc(int32_t device, const gq_tensor_t* tensors, int32_t 
     }
     if (host_diags != nullptr && count > 0) {
         st = cuda_status(cudaMemcpyAsync(host_diags, d_diag, sizeof(gq_diag_t) * count, cudaMemcpyDeviceToHost, s));
-        if (st != GQ_OK) return st;
+        if (st != GQ_OK) return fail(st);
     }
     return cuda_status(cudaStreamSynchronize(s));
 }

@@ -31,23 +31,11 @@ __device__ __forceinline__ int f32_to_i16_x86(float x) {
 
 // ---- global memory --------------------------------------------------------------------
 
-// Output stores name the global state space (st.global) rather than going through a
+// Output stores name the global state space (st.global.wb) rather than going through a
 // generic pointer, so that the compiler knows they cannot alias the shared-memory tiles.
-// Policy: 1 write-back (default), 2 cache-global, 3 streaming.
-#ifndef GQ_STORE_POLICY
-#define GQ_STORE_POLICY 1
-#endif
 template <class T>
 __device__ __forceinline__ void st_global(T* p, T v) {
-#if GQ_STORE_POLICY == 3
-    __stcs(p, v);
-#elif GQ_STORE_POLICY == 2
-    __stcg(p, v);
-#elif GQ_STORE_POLICY == 1
     __stwb(p, v);
-#else
-    *p = v;
-#endif
 }
 __device__ __forceinline__ void stg128(void* p, uint4 v) { st_global(reinterpret_cast<uint4*>(p), v); }
 __device__ __forceinline__ void stg128f(float* p, float a, float b, float c, float d) {
@@ -59,10 +47,6 @@ template <int MODE, class T>
 __device__ __forceinline__ void st_out(T* p, T v);
 
 // ---- per-block requantization parameters (requantize_symmetric) --------------------
-
-#ifndef GQ_RQ_BRANCHLESS
-#define GQ_RQ_BRANCHLESS 1
-#endif
 
 // f32(f16(1e-4)): SCALE_EPSILON of ggml_quant.py:836 widened exactly (f16 bits 0x068E).
 constexpr float kScaleEpsilon = 1.0001659393310547e-4f;
@@ -102,7 +86,6 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     // since rounding is monotone the rounded quotient of the smaller one is the minimum.
     const bool need_lo = lo < static_cast<float>(lo_out) / 16.0f;
     const bool need_hi = hi > static_cast<float>(hi_out) / 16.0f;
-#if GQ_RQ_BRANCHLESS
     // the candidate quotient is computed unconditionally and selected, which keeps the
     // dependent chain free of divergent branches (the quotient is discarded when neither
     // bound applies; its operands are then finite or the result is unused)
@@ -112,38 +95,15 @@ __device__ __forceinline__ Requant requant_block(float S, float M, int qmin, int
     float sf = (need_lo || need_hi) ? fminf(16.0f, t) : 16.0f;
     const bool big = sf > 0.98f;
     sf = big ? fmaxf(floorf(sf), 1.0f) : sf;
-#else
-    float sf = 16.0f;
-    if (need_lo || need_hi) {
-        const float e = __fmaf_rn(-static_cast<float>(hi_out), lo, __fmul_rn(static_cast<float>(lo_out), hi));
-        const bool use_lo = need_lo && (!need_hi || e > 0.0f);
-        sf = fminf(sf, __fdiv_rn(static_cast<float>(use_lo ? lo_out : hi_out), use_lo ? lo : hi));
-    }
-    const bool big = sf > 0.98f;
-    if (big) sf = fmaxf(floorf(sf), 1.0f);
-#endif
     const float rmv = __fmul_rn(r, sf);
     const int rm = __float2int_rn(rmv);
     p.sf = sf;
     p.rm = rm;
     p.round_err = fabsf(__fsub_rn(rintf(rmv), rmv));
     p.fast = big || (sf == 0.0f);
-    int vmin, vmax;
-#if GQ_RQ_BRANCHLESS
     p.sfi = p.fast ? static_cast<int>(sf) : 0;
-    vmin = (p.fast ? qmin * p.sfi : __float2int_rn(__fmul_rn(qminf, sf))) + rm;
-    vmax = (p.fast ? qmax * p.sfi : __float2int_rn(__fmul_rn(qmaxf, sf))) + rm;
-#else
-    if (p.fast) {
-        p.sfi = static_cast<int>(sf);
-        vmin = qmin * p.sfi + rm;
-        vmax = qmax * p.sfi + rm;
-    } else {
-        p.sfi = 0;
-        vmin = __float2int_rn(__fmul_rn(qminf, sf)) + rm;
-        vmax = __float2int_rn(__fmul_rn(qmaxf, sf)) + rm;
-    }
-#endif
+    const int vmin = (p.fast ? qmin * p.sfi : __float2int_rn(__fmul_rn(qminf, sf))) + rm;
+    const int vmax = (p.fast ? qmax * p.sfi : __float2int_rn(__fmul_rn(qmaxf, sf))) + rm;
     // scale = S / sf (the original S, ggml_quant.py:882).  For an integer sf in 1..16 and a
     // finite S: q0 = S*(1/sf) and one fma correction, which equals IEEE division for every
     // f16-derived S (checked exhaustively, tests/numerics/div_by_small_int.c).

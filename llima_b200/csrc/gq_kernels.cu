@@ -176,38 +176,16 @@ struct GroupWords {
     uint32_t h[Q5 ? 8 : 1];
 };
 
-// a & m that the compiler may not merge with an equal expression elsewhere: the masks are
-// recomputed where they are used instead of being kept live across the requantization
-__device__ __forceinline__ uint32_t and_fresh(uint32_t a, uint32_t m) {
-    uint32_t r;
-    asm volatile("and.b32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(m));
-    return r;
-}
-
-// Recompute the lane layouts in the apply phase instead of keeping them live (1), or let
-// the compiler keep them (0).
-#ifndef GQ_FRESH_MASKS
-#define GQ_FRESH_MASKS 0
-#endif
-
-// The four 16-bit lane layouts of word i (see above).  FRESH: recompute (apply phase).
-template <bool Q5, bool FRESH_ = false>
+// The four 16-bit lane layouts of word i (see above).
+template <bool Q5>
 __device__ __forceinline__ void group_layouts(const GroupWords<Q5>& q, int i, uint32_t& el, uint32_t& ol,
                                               uint32_t& eh, uint32_t& oh) {
-    constexpr bool FRESH = FRESH_ && GQ_FRESH_MASKS;
     const uint32_t w = q.w[i];
     if (!Q5) {
-        if (FRESH) {
-            el = and_fresh(w, 0x000F000Fu);
-            ol = and_fresh(w, 0x0F000F00u);
-            eh = and_fresh(w, 0x00F000F0u);
-            oh = and_fresh(w, 0xF000F000u);
-        } else {
-            el = w & 0x000F000Fu;
-            ol = w & 0x0F000F00u;
-            eh = w & 0x00F000F0u;
-            oh = w & 0xF000F000u;
-        }
+        el = w & 0x000F000Fu;
+        ol = w & 0x0F000F00u;
+        eh = w & 0x00F000F0u;
+        oh = w & 0xF000F000u;
     } else {
         const uint32_t t = q.h[Q5 ? i : 0], t4 = t << 4;
         el = (w & 0x000F000Fu) | (t4 & 0x00100010u);
@@ -355,7 +333,7 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
             // (EH*sf + 16K) >> 4 and high32(OH * (sf << 20)) + K (Q5_K: OH*sf + K); the
             // low bytes of the 16-bit lanes are the codes (the bias has a zero low byte)
             uint32_t el, ol, eh, oh;
-            group_layouts<Q5, true>(q, i, el, ol, eh, oh);
+            group_layouts(q, i, el, ol, eh, oh);
             lo[i] = codes_word(el * sfiL + KL, mad_hi(ol, sfiL << 24, KL));
             hi[i] = codes_word((eh * sfiH + (KH << 4)) >> 4, Q5 ? oh * sfiH + KH : mad_hi(oh, sfiH << 20, KH));
         }
@@ -419,7 +397,7 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             uint32_t el, ol, eh, oh;
-            group_layouts<Q5, true>(q, i, el, ol, eh, oh);
+            group_layouts(q, i, el, ol, eh, oh);
             const uint32_t ql = codes_word(el, ol >> 8);
             const uint32_t qh = codes_word(eh >> 4, oh >> kOHShift);
             stg128f(vdst + 4 * i, __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 0))), dmL),

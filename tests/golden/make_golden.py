@@ -101,7 +101,7 @@ def _nonfinite(fmt: str, n_units: int, seed: int) -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="the reference checkout (the directory holding sima_lmm/)")
     ap.add_argument("--out", default=str(HERE))
     ap.add_argument("--only", choices=["all", "partition", "ggml_quant"], default="all",
                     help="partition: rewrite only partition.json; ggml_quant: only ggml_quant/*.npz")

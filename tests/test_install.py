@@ -25,7 +25,9 @@ import pytest
 from llima_b200.synth import gen_tensor_bytes
 from oracle import ggml_oracle as O
 
-REFERENCE = Path(os.environ.get("LLIMA_REFERENCE", "/root/reference"))
+# the reference checkout (the directory holding sima_lmm/), named by LLIMA_REFERENCE; the
+# tests that import it skip when the variable is unset
+REFERENCE = Path(os.environ["LLIMA_REFERENCE"]) if os.environ.get("LLIMA_REFERENCE") else None
 
 # name -> (format, rows, cols): a one-layer llama file, 4 heads of 64, 2 kv heads
 TENSORS = {
@@ -60,8 +62,8 @@ def _write_gguf(path: Path):
 
 
 def _import_reference():
-    if not (REFERENCE / "sima_lmm" / "gguf" / "gguf_conversion.py").exists():
-        pytest.skip("reference checkout not available")
+    if REFERENCE is None or not (REFERENCE / "sima_lmm" / "gguf" / "gguf_conversion.py").exists():
+        pytest.skip("reference checkout not available (set LLIMA_REFERENCE)")
     if str(REFERENCE) not in sys.path:
         sys.path.append(str(REFERENCE))   # after this repository: its `tests` must win
     sys.modules.setdefault("llama_cpp", types.SimpleNamespace(Llama=object))

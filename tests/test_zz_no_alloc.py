@@ -115,3 +115,25 @@ def test_noalloc_rejects_requests_beyond_its_array():
     t.perm_heads = 0
     assert lib.gq_convert_host_noalloc(0, ctypes.byref(t), 1, N.OUT_CODES, None, None) == 0
     assert not codes.any() and not scales.any()
+
+
+def test_noalloc_warm_up_call_and_a_user_stream():
+    import torch
+    lib = N.lib()
+    # a call with no tensors loads the library's device code and reserves the array, and
+    # converts nothing (the warm-up a caller makes before handing memory to another allocator)
+    assert lib.gq_convert_host_noalloc(0, None, 0, N.OUT_CODES, None, None) == 0
+    want = _session_result(3, N.OUT_CODES)
+    dev_before = torch.cuda.current_device()
+    stream = torch.cuda.Stream(device=0)
+    for _ in range(2):
+        hs = HostSet(3, N.OUT_CODES)
+        N.check(lib.gq_convert_host_noalloc(0, hs.records, len(SPECS), N.OUT_CODES, hs.diags,
+                                            ctypes.c_void_p(stream.cuda_stream)), "gq_convert_host_noalloc")
+        got = hs.outputs()
+        assert got[1] == want[1]
+        for spec, a, b in zip(SPECS, want[0], got[0]):
+            for name in a:
+                assert np.array_equal(a[name].view(np.uint8), b[name].view(np.uint8)), (spec, name)
+    # the call leaves the caller's current device as it found it
+    assert torch.cuda.current_device() == dev_before
