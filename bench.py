@@ -801,7 +801,7 @@ def run_ours(args, rank, world, local_rank):
     full_set = not (args.layers or args.formats) and out_mask == N.OUT_CODES
     peak_, _ = measured_peak()
     configs = None
-    if not args.no_configs and full_set:
+    if not args.no_configs and out_mask == N.OUT_CODES:
         from llima_b200.synth import model_specs
         configs = {}
         for key, fmt, rows, cols in (("C1_Q8_0_4096x4096", "Q8_0", 4096, 4096),

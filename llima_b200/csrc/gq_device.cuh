@@ -19,6 +19,13 @@ __device__ __forceinline__ float h2f(uint32_t bits) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xFFFFu)));
 }
 
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t w) {
+    __half2 h;
+    static_assert(sizeof(h) == sizeof(w), "half2 is 32 bits");
+    memcpy(&h, &w, sizeof(w));
+    return h;
+}
+
 // numpy's f32 -> f16 astype: round to nearest even, overflow to inf, subnormals kept.
 __device__ __forceinline__ float round_to_f16(float x) { return __half2float(__float2half_rn(x)); }
 
@@ -40,6 +47,14 @@ __device__ __forceinline__ void st_global(T* p, T v) {
 __device__ __forceinline__ void stg128(void* p, uint4 v) { st_global(reinterpret_cast<uint4*>(p), v); }
 __device__ __forceinline__ void stg128f(float* p, float a, float b, float c, float d) {
     st_global(reinterpret_cast<float4*>(p), make_float4(a, b, c, d));
+}
+
+// 32 bytes to a 32-byte-aligned global address in one store (sm_100's 256-bit st.global):
+// a warp of such stores writes whole 32-byte sectors.
+__device__ __forceinline__ void stg256(void* p, const uint32_t (&w)[8]) {
+    asm volatile("st.global.wb.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+                 "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
 }
 
 // Code / scale store of a conversion (defined with the shared-memory helpers below).
@@ -347,6 +362,61 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src,
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
+
+// ---- bulk copies (the TMA engine) into shared memory, completed on an mbarrier --------
+//
+// One lane issues a whole tile as a single 1-D bulk copy from this GPU's global memory
+// (no cluster multicast); the warp waits on the stage's mbarrier phase.  The copy engine
+// keeps far more bytes in flight per SM than per-lane 16-byte copies can.
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32addr(bar)), "r"(count) : "memory");
+}
+// makes barrier initialisation visible to the copy engine (before the CTA-wide barrier)
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// `bytes` (a multiple of 16) from 16-byte-aligned global `src` to 16-byte-aligned shared `dst`
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Every wait on a copy ends: after kWaitLimitNs of global time without the phase completing,
+// the wait gives up and returns false (the kernel then records kErrWaitTimeout and stops).
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+constexpr unsigned kErrWaitTimeout = 1u;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_ns() - t0 > kWaitLimitNs) return false;
+    }
+    return true;
+}
 
 // ---- code / scale stores of a conversion ---------------------------------------------
 

@@ -61,7 +61,14 @@ namespace gq {
 template <int TYPE>
 struct Fmt;
 
-#define GQ_FMT(TYPE, UNIT_BYTES, UNITS_PER_TILE, STAGES, WARPS)                           \
+#ifndef GQ_Q6K_BULK
+#define GQ_Q6K_BULK 0
+#endif
+#ifndef GQ_Q0_BULK
+#define GQ_Q0_BULK 1
+#endif
+
+#define GQ_FMT(TYPE, UNIT_BYTES, UNITS_PER_TILE, STAGES, WARPS, BULK)                     \
     template <>                                                                           \
     struct Fmt<TYPE> {                                                                    \
         static constexpr int kWarps = WARPS;  /* warps per CTA */                         \
@@ -71,19 +78,21 @@ struct Fmt;
         static constexpr int kTileBytes = UNIT_BYTES * UNITS_PER_TILE;                    \
         static constexpr int kStageBytes = kTileBytes + 16; /* slack for 20-byte reads */ \
         static constexpr int kStages = STAGES;                                            \
+        /* tiles arrive by one bulk copy each, or by 16-byte copies of every lane */      \
+        static constexpr bool kBulk = BULK;                                               \
         static_assert(kTileBytes % 16 == 0, "tiles must be whole 16-byte chunks");        \
     };
 
-GQ_FMT(GQ_TYPE_Q4_K, 144, 8 * GQ_K45_SUB, GQ_K45_STAGES, GQ_K45_WARPS)   // sub-tiles of 8 super-blocks
-GQ_FMT(GQ_TYPE_Q5_K, 176, 8 * GQ_Q5K_SUB, GQ_Q5K_STAGES, GQ_Q5K_WARPS)
-GQ_FMT(GQ_TYPE_Q6_K, 210, 8 * GQ_Q6K_SUB, GQ_Q6K_STAGES, 8)   // sub-tiles of 128 blocks of 16
-GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4, 8)   // 32 blocks of 32 per tile
-GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4, 8)
-GQ_FMT(GQ_TYPE_Q4_1, 20, 32, 4, 8)   // 32 blocks of 32 per tile, one per lane
-GQ_FMT(GQ_TYPE_Q5_0, 22, 32, 4, 8)
-GQ_FMT(GQ_TYPE_Q5_1, 24, 32, 4, 8)
-GQ_FMT(GQ_TYPE_Q2_K, 84, 8, 4, 8)    // 128 blocks of 16 per tile, one per lane and round
-GQ_FMT(GQ_TYPE_Q3_K, 110, 8, 4, 8)
+GQ_FMT(GQ_TYPE_Q4_K, 144, 8 * GQ_K45_SUB, GQ_K45_STAGES, GQ_K45_WARPS, true)   // sub-tiles of 8 super-blocks
+GQ_FMT(GQ_TYPE_Q5_K, 176, 8 * GQ_Q5K_SUB, GQ_Q5K_STAGES, GQ_Q5K_WARPS, true)
+GQ_FMT(GQ_TYPE_Q6_K, 210, 8 * GQ_Q6K_SUB, GQ_Q6K_STAGES, 8, GQ_Q6K_BULK)   // sub-tiles of 128 blocks of 16
+GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4, 8, GQ_Q0_BULK)   // 32 blocks of 32 per tile
+GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4, 8, GQ_Q0_BULK)
+GQ_FMT(GQ_TYPE_Q4_1, 20, 32, 4, 8, GQ_Q0_BULK)   // 32 blocks of 32 per tile, one per lane
+GQ_FMT(GQ_TYPE_Q5_0, 22, 32, 4, 8, GQ_Q0_BULK)
+GQ_FMT(GQ_TYPE_Q5_1, 24, 32, 4, 8, GQ_Q0_BULK)
+GQ_FMT(GQ_TYPE_Q2_K, 84, 8, 4, 8, GQ_Q0_BULK)    // 128 blocks of 16 per tile, one per lane and round
+GQ_FMT(GQ_TYPE_Q3_K, 110, 8, 4, 8, GQ_Q0_BULK)
 #undef GQ_FMT
 
 // Minimum resident CTAs per SM the Q4_K kernel is compiled for (caps its registers; the
@@ -132,6 +141,33 @@ __device__ __forceinline__ void issue_tile(const GqBatch& b, DescCursor& cur, in
         cp_async16(stage + c, src + c, n < 16 ? n : 16);
     }
 }
+
+// Tile `t` as one bulk copy into `stage`, completed on `bar` (lane 0 only; nothing when t is
+// past the end).  A whole tile is a multiple of 16 bytes, so every tile starts 16-byte
+// aligned (the tensor's bytes do); the last tile of a tensor may end with fewer than 16
+// bytes past its last whole chunk, which lane 0 copies itself before it arrives on the
+// barrier (the arrival releases those stores to the lanes that wait on it).
+template <class F>
+__device__ __forceinline__ void issue_tile_bulk(const GqBatch& b, DescCursor& cur, int64_t t, uint8_t* stage,
+                                                uint64_t* bar) {
+    if (t >= b.total_tiles) return;
+    const GqDesc& d = b.d[cur.seek(b, t)];
+    const int64_t unit0 = (t - d.tile_begin) * F::kUnitsPerTile;
+    const int64_t left = d.n_units - unit0;
+    const int nunits = left < F::kUnitsPerTile ? static_cast<int>(left) : F::kUnitsPerTile;
+    const uint32_t nbytes = static_cast<uint32_t>(nunits * F::kUnitBytes);
+    const uint32_t whole = nbytes & ~15u;
+    const uint8_t* src = d.src + unit0 * F::kUnitBytes;
+    if (F::kUnitBytes % 16 != 0) {
+        for (uint32_t i = whole; i < nbytes; ++i) stage[i] = src[i];
+    }
+    mbar_arrive_expect_tx(bar, whole);
+    if (whole != 0) bulk_load(stage, src, whole, bar);
+}
+
+// Sticky error flags of this device's conversion kernels (kErrWaitTimeout: a tile copy did
+// not complete within the wait limit, so the launch stopped early).
+__device__ unsigned int gq_kernel_errors;
 
 // ---------------------------------------------------------------------------------------
 // Q4_K / Q5_K: 256-value super-blocks -> 8 blocks of 32, asymmetric -> symmetric int8
@@ -193,6 +229,25 @@ __device__ __forceinline__ void group_layouts(const GroupWords<Q5>& q, int i, ui
         eh = (w & 0x00F000F0u) | ((t << 7) & 0x01000100u);
         oh = ((w >> 12) & 0x000F000Fu) | ((t >> 5) & 0x00100010u);
     }
+}
+
+// The constants of a lane's two blocks, S = f16(sc * d) and P = f16(m * dmin), from the
+// 6-bit pairs sc2 = scL | scH << 8, mn2 = mnL | mnH << 8 and the header word (d | dmin << 16).
+// The f32 product of a 6-bit integer and an f16 value is exact, so rounding it to f16 (what
+// remove_superblocks does, ggml_quant.py:771-777) equals one correctly rounded f16 multiply:
+// both blocks' products are one mul.rn.f16x2 each for S and P, with the integers made f16 by
+// the bias trick (f16 bits 0x6400 | k = 1024 + k for k < 1024, minus 1024, exactly).
+__device__ __forceinline__ void block_constants_h2(uint32_t sc2, uint32_t mn2, uint32_t hdr, float& SL, float& SH,
+                                                   float& PL, float& PH) {
+    const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400u), __ushort_as_half(0x6400u));
+    const __half2 scf = __hsub2(u32_as_h2(__byte_perm(sc2, 0x6464u, 0x4140u)), k1024);
+    const __half2 mnf = __hsub2(u32_as_h2(__byte_perm(mn2, 0x6464u, 0x4140u)), k1024);
+    const __half2 s2 = __hmul2_rn(scf, u32_as_h2(__byte_perm(hdr, 0u, 0x1010u)));
+    const __half2 p2 = __hmul2_rn(mnf, u32_as_h2(__byte_perm(hdr, 0u, 0x3232u)));
+    SL = __low2float(s2);
+    SH = __high2float(s2);
+    PL = __low2float(p2);
+    PH = __high2float(p2);
 }
 
 // Block constants of block b (0..7) of a Q4_K / Q5_K super-block, read by every lane of
@@ -280,8 +335,10 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
         }
     }
 
-    const int64_t ou = permute_unit(D, unit0 + sb);
-    const int64_t off = ou * 256 + 64 * g;   // codes / values of block 2g, then 2g+1
+    // codes / values of block 2g, then 2g+1: unit ou, byte 64g of it (unpermuted, the
+    // warp's 8 units are consecutive and lane l writes bytes 64l.. of them); the block
+    // scales of the pair sit at off / 32
+    const int64_t off = D.perm_heads == 0 ? unit0 * 256 + 64 * lane : permute_unit(D, unit0 + sb) * 256 + 64 * g;
     if (MODE & kOutCodes) {
         // block min / max of the codes (16-bit-lane SIMD), two words per step
         uint32_t mnEL, mxEL, mnOL, mxOL, mnEH, mxEH, mnOH, mxOH;
@@ -312,14 +369,12 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
 
         // block constants f16(f32 product), min negated (ggml_quant.py:771-777), then
         // requantize_symmetric (ggml_quant.py:785-886) for the common case (P = -M)
-        const float SL = round_to_f16(__fmul_rn(static_cast<float>(scL), d));
-        const float SH = round_to_f16(__fmul_rn(static_cast<float>(scH), d));
-        const float PL = round_to_f16(__fmul_rn(static_cast<float>(mnL), dmin));
-        const float PH = round_to_f16(__fmul_rn(static_cast<float>(mnH), dmin));
+        float SL, SH, PL, PH;
+        block_constants_h2(sc2, mn2, hdr, SL, SH, PL, PH);
         const FastRequant pL = requant_fast(SL, PL, qminL, qmaxL, recip);
         const FastRequant pH = requant_fast(SH, PH, qminH, qmaxH, recip);
         if (valid) {
-            st_out<MODE>(reinterpret_cast<float2*>(D.scales + ou * 8 + 2 * g), make_float2(pL.scale, pH.scale));
+            st_out<MODE>(reinterpret_cast<float2*>(D.scales + (off >> 5)), make_float2(pL.scale, pH.scale));
             acc.add(fmaxf(pL.round_err, pH.round_err), 0);
         }
         constexpr uint32_t kBias = 0x400u;   // lane value q*sf + rm + bias stays in [0, 4096)
@@ -338,13 +393,19 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
             hi[i] = codes_word((eh * sfiH + (KH << 4)) >> 4, Q5 ? oh * sfiH + KH : mad_hi(oh, sfiH << 20, KH));
         }
         uint8_t* base = D.codes + off;
-        if (valid && pL.good) {
-            st_out128<MODE>(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
-            st_out128<MODE>(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
-        }
-        if (valid && pH.good) {
-            st_out128<MODE>(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
-            st_out128<MODE>(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
+        if ((MODE & kOutSmem) == 0 && (reinterpret_cast<uintptr_t>(D.codes) & 31u) == 0) {
+            // a block's 32 codes as one 32-byte store: whole sectors, half the instructions
+            if (valid && pL.good) stg256(base, lo);
+            if (valid && pH.good) stg256(base + 32, hi);
+        } else {
+            if (valid && pL.good) {
+                st_out128<MODE>(base, make_uint4(lo[0], lo[1], lo[2], lo[3]));
+                st_out128<MODE>(base + 16, make_uint4(lo[4], lo[5], lo[6], lo[7]));
+            }
+            if (valid && pH.good) {
+                st_out128<MODE>(base + 32, make_uint4(hi[0], hi[1], hi[2], hi[3]));
+                st_out128<MODE>(base + 48, make_uint4(hi[4], hi[5], hi[6], hi[7]));
+            }
         }
         // the other blocks (about 0.5%): one warp pass each, after the scale stores above;
         // a block with finite constants is finished from its lane's r and sf0, one with a
@@ -708,13 +769,21 @@ __global__ void __launch_bounds__(Fmt<TYPE>::kThreads,
                                   TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS : (TYPE == GQ_TYPE_Q5_K ? 2 : 1))
     gq_convert_kernel(const __grid_constant__ GqBatch batch) {
     using F = Fmt<TYPE>;
+    constexpr bool kBulk = F::kBulk;
     extern __shared__ __align__(16) uint8_t smem[];
     // exact reciprocals 1/k, k = 1..16, for the block-scale division of requant_block
     __shared__ float recip[17];
-    if (threadIdx.x < 17) recip[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, static_cast<float>(threadIdx.x)) : 0.0f;
-    __syncthreads();
+    // one mbarrier per stage of each warp's ring (bulk-copy formats)
+    __shared__ uint64_t bars[kBulk ? F::kWarps * F::kStages : 1];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
+    uint64_t* wbar = bars + (kBulk ? warp * F::kStages : 0);
+    if (threadIdx.x < 17) recip[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, static_cast<float>(threadIdx.x)) : 0.0f;
+    if (kBulk && lane == 0) {
+        for (int s = 0; s < F::kStages; ++s) mbar_init(&wbar[s], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
     uint8_t* ring = smem + warp * (F::kStages * F::kStageBytes);
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * F::kWarps;
     const int64_t first = static_cast<int64_t>(blockIdx.x) * F::kWarps + warp;
@@ -724,20 +793,44 @@ __global__ void __launch_bounds__(Fmt<TYPE>::kThreads,
     int64_t t_issue = first;
 #pragma unroll
     for (int s = 0; s < F::kStages - 1; ++s) {
-        issue_tile<F>(batch, issue_cur, t_issue, ring + s * F::kStageBytes, lane);
-        cp_async_commit();
+        if constexpr (kBulk) {
+            if (lane == 0) issue_tile_bulk<F>(batch, issue_cur, t_issue, ring + s * F::kStageBytes, &wbar[s]);
+        } else {
+            issue_tile<F>(batch, issue_cur, t_issue, ring + s * F::kStageBytes, lane);
+            cp_async_commit();
+        }
         t_issue += nwarps;
     }
 
     DiagAcc acc;
     int stage = 0;
+    uint32_t phase = 0;   // bit s: parity of stage s's next completion
     for (int64_t t = first; t < total; t += nwarps) {
-        cp_async_wait<F::kStages - 2>();
-        __syncwarp();
+        if constexpr (kBulk) {
+            const bool ok = mbar_wait(&wbar[stage], (phase >> stage) & 1u);
+            if (__any_sync(kFull, !ok)) {
+                // give up: record it, let the copies still owed to this warp's ring land
+                // (each wait again bounded), and stop
+                if (lane == 0) atomicOr(&gq_kernel_errors, kErrWaitTimeout);
+                for (int k = 0; k < F::kStages - 1; ++k) {
+                    const int s = (stage + k) % F::kStages;
+                    if (t + k * nwarps < total) mbar_wait(&wbar[s], (phase >> s) & 1u);
+                }
+                break;
+            }
+            phase ^= 1u << stage;
+        } else {
+            cp_async_wait<F::kStages - 2>();
+            __syncwarp();
+        }
         // refill the stage consumed in the previous iteration
         const int refill = (stage == 0) ? F::kStages - 1 : stage - 1;
-        issue_tile<F>(batch, issue_cur, t_issue, ring + refill * F::kStageBytes, lane);
-        cp_async_commit();
+        if constexpr (kBulk) {
+            if (lane == 0) issue_tile_bulk<F>(batch, issue_cur, t_issue, ring + refill * F::kStageBytes, &wbar[refill]);
+        } else {
+            issue_tile<F>(batch, issue_cur, t_issue, ring + refill * F::kStageBytes, lane);
+            cp_async_commit();
+        }
         t_issue += nwarps;
 
         const GqDesc& D = batch.d[proc_cur.seek(batch, t)];
@@ -773,7 +866,7 @@ __global__ void __launch_bounds__(Fmt<TYPE>::kThreads,
         __syncwarp();
         stage = (stage + 1 == F::kStages) ? 0 : stage + 1;
     }
-    cp_async_wait<0>();
+    if constexpr (!kBulk) cp_async_wait<0>();
     if ((MODE & kOutCodes) && (TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K || TYPE == GQ_TYPE_Q4_1 ||
                                TYPE == GQ_TYPE_Q5_0 || TYPE == GQ_TYPE_Q5_1 || TYPE == GQ_TYPE_Q2_K ||
                                TYPE == GQ_TYPE_Q3_K))
