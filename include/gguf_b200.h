@@ -48,7 +48,7 @@
 extern "C" {
 #endif
 
-#define GQ_ABI_VERSION 1
+#define GQ_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define GQ_API __attribute__((visibility("default")))
@@ -125,6 +125,16 @@ GQ_API int gq_version(void);
 GQ_API const char* gq_strerror(int status);
 /* CUDA error code (cudaError_t) behind the last GQ_ERR_CUDA of the calling thread. */
 GQ_API int gq_last_cuda_error(void);
+
+/* Sticky error flags of the conversion kernels on `device`, or-ed over every launch since
+ * the last clear.  GQ_KERNEL_WAIT_TIMEOUT: a kernel waited about a second for a tile copy
+ * that did not complete and stopped early, so that launch's outputs are incomplete.  The
+ * flags live in device memory: read them once the work they should cover has finished.
+ * clear != 0 resets them.  No counterpart in the reference (whose numpy path cannot stall).
+ * gq_convert_host and gq_convert_host_noalloc read and clear them themselves and fail with
+ * GQ_ERR_CUDA (gq_last_cuda_error() = cudaErrorTimeout) when a flag was set. */
+#define GQ_KERNEL_WAIT_TIMEOUT 1u
+GQ_API int gq_kernel_errors(int32_t device, int32_t clear, uint32_t* flags);
 
 GQ_API int gq_query(int32_t type, int64_t rows, int64_t cols, gq_layout_t* out);
 

@@ -31,6 +31,30 @@ int cuda_status(cudaError_t e) {
 }
 int cuda_status(int e) { return cuda_status(static_cast<cudaError_t>(e)); }
 
+// Makes `device` current for one entry-point call and puts the caller's current device
+// back on every return path (hosts such as torch keep their own notion of it).
+class DeviceScope {
+public:
+    explicit DeviceScope(int device) {
+        status_ = cuda_status(cudaGetDevice(&prev_));
+        if (status_ == GQ_OK && prev_ != device) {
+            status_ = cuda_status(cudaSetDevice(device));
+            switched_ = status_ == GQ_OK;
+        }
+    }
+    ~DeviceScope() {
+        if (switched_) cudaSetDevice(prev_);
+    }
+    DeviceScope(const DeviceScope&) = delete;
+    DeviceScope& operator=(const DeviceScope&) = delete;
+    int status() const { return status_; }
+
+private:
+    int prev_ = 0;
+    int status_ = GQ_OK;
+    bool switched_ = false;
+};
+
 struct TypeInfo {
     int unit_values;
     int unit_bytes;
@@ -172,6 +196,14 @@ const char* gq_strerror(int status) {
 }
 
 int gq_last_cuda_error(void) { return g_last_cuda; }
+
+int gq_kernel_errors(int32_t device, int32_t clear, uint32_t* flags) {
+    if (flags == nullptr) return GQ_ERR_NULL;
+    *flags = 0;
+    const DeviceScope scope(device);
+    if (scope.status() != GQ_OK) return scope.status();
+    return cuda_status(gq::kernel_errors(clear != 0, flags));
+}
 
 int gq_query(int32_t type, int64_t rows, int64_t cols, gq_layout_t* out) {
     if (out == nullptr) return GQ_ERR_NULL;
@@ -673,6 +705,15 @@ struct gq_session {
 
 namespace {
 
+// After a call's work has finished: GQ_OK, or GQ_ERR_CUDA (cudaErrorTimeout) when a
+// conversion kernel on the current device gave up waiting for a copy (flags cleared).
+int kernels_ok() {
+    uint32_t flags = 0;
+    const int e = gq::kernel_errors(true, &flags);
+    if (e != 0) return cuda_status(e);
+    return flags != 0 ? cuda_status(cudaErrorTimeout) : GQ_OK;
+}
+
 constexpr size_t kAlign = 256;
 size_t round_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 
@@ -691,29 +732,6 @@ struct Member {
     int64_t units;
 };
 
-// Makes `device` current for one entry-point call and puts the caller's current device
-// back on every return path (hosts such as torch keep their own notion of it).
-class DeviceScope {
-public:
-    explicit DeviceScope(int device) {
-        status_ = cuda_status(cudaGetDevice(&prev_));
-        if (status_ == GQ_OK && prev_ != device) {
-            status_ = cuda_status(cudaSetDevice(device));
-            switched_ = status_ == GQ_OK;
-        }
-    }
-    ~DeviceScope() {
-        if (switched_) cudaSetDevice(prev_);
-    }
-    DeviceScope(const DeviceScope&) = delete;
-    DeviceScope& operator=(const DeviceScope&) = delete;
-    int status() const { return status_; }
-
-private:
-    int prev_ = 0;
-    int status_ = GQ_OK;
-    bool switched_ = false;
-};
 
 // Pinned bounce slots and the copy pool, on the first request with a pageable buffer.
 // Without them (pinned allocation refused) pageable buffers are handed to the copy
@@ -1035,6 +1053,7 @@ int gq_convert_host(gq_session_t* s, const gq_tensor_t* tensors, int32_t count, 
         if (st != GQ_OK) return fail(st);
     }
     if (s->prefault) s->prefault->cancel();
+    if ((st = kernels_ok()) != GQ_OK) return st;
     if (host_diags != nullptr && count > 0) {
         // every stream's kernels have finished: read the maxima
         st = cuda_status(cudaMemcpy(host_diags, s->d_diag, sizeof(gq_diag_t) * count, cudaMemcpyDeviceToHost));
@@ -1232,7 +1251,8 @@ int gq_convert_host_noalloc(int32_t device, const gq_tensor_t* tensors, int32_t 
         st = cuda_status(cudaMemcpyAsync(host_diags, d_diag, sizeof(gq_diag_t) * count, cudaMemcpyDeviceToHost, s));
         if (st != GQ_OK) return fail(st);
     }
-    return cuda_status(cudaStreamSynchronize(s));
+    if ((st = cuda_status(cudaStreamSynchronize(s))) != GQ_OK) return st;
+    return kernels_ok();
 }
 
 }  // extern "C"

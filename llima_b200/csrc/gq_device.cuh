@@ -407,7 +407,7 @@ __device__ __forceinline__ uint64_t global_ns() {
 // Every wait on a copy ends: after kWaitLimitNs of global time without the phase completing,
 // the wait gives up and returns false (the kernel then records kErrWaitTimeout and stops).
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
-constexpr unsigned kErrWaitTimeout = 1u;
+constexpr unsigned kErrWaitTimeout = GQ_KERNEL_WAIT_TIMEOUT;
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;

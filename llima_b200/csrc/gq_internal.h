@@ -74,6 +74,8 @@ struct GqModalixBatch {
 };
 
 // launch entry points implemented in gq_kernels.cu
+// sticky kernel error flags of the current device (read, then cleared when `clear`)
+int kernel_errors(bool clear, uint32_t* flags);
 int launch_batch(int type, int out_mask, const GqBatch& batch, void* stream);
 int64_t tiles_for(int type, int64_t n_units);
 int launch_modalix(int type, const GqModalixBatch& b, void* stream);

@@ -1294,6 +1294,17 @@ int launch_modalix_t(const GqModalixBatch& m, cudaStream_t s) {
 
 }  // namespace
 
+int kernel_errors(bool clear, uint32_t* flags) {
+    unsigned v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, gq_kernel_errors, sizeof(v));
+    if (e == cudaSuccess && clear && v != 0) {
+        const unsigned zero = 0;
+        e = cudaMemcpyToSymbol(gq_kernel_errors, &zero, sizeof(zero));
+    }
+    *flags = v;
+    return static_cast<int>(e);
+}
+
 int launch_modalix(int type, const GqModalixBatch& m, void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (type) {

@@ -22,7 +22,7 @@ def test_library_exports_every_declared_symbol():
     lib = N.lib()
     for name in declared:
         assert hasattr(lib, name)
-    assert lib.gq_version() == 1
+    assert lib.gq_version() == 2
 
 
 def test_strerror_and_query():
