@@ -10,8 +10,8 @@ the reference so that results are bit-identical:
 * block constants of K-quants are ``f16(f32(int) * f32(f16))`` (one f32 product, then
   round-to-nearest-even to f16), ``sima_lmm/gguf/ggml_quant.py:771-777``;
 * ``requantize_symmetric`` works in f32 throughout, ``ggml_quant.py:785-886``;
-* float -> int16 casts follow numpy on x86-64 (via int32; NaN and out-of-range
-  values become 0), which matters only for non-finite intermediates.
+* float -> int16 casts are numpy's own, as in the reference (on x86-64 through int32;
+  NaN and out-of-range values become 0), which matters only for non-finite values.
 
 Pinning: ``tests/golden/make_golden.py`` runs the reference functions themselves on
 seeded inputs and commits their outputs under ``tests/golden/``;
@@ -81,6 +81,8 @@ def _units(data, fmt: Format) -> np.ndarray:
 
 def _f16_field(units: np.ndarray, offset: int) -> np.ndarray:
     """f16 stored little-endian at byte ``offset`` of each unit, widened to f32 (exact)."""
+    if offset % 2 == 0 and units.shape[1] % 2 == 0 and units.flags.c_contiguous:
+        return units.view(np.float16)[:, offset // 2].astype(np.float32)
     return np.ascontiguousarray(units[:, offset:offset + 2]).view(np.float16)[:, 0].astype(np.float32)
 
 
@@ -182,25 +184,28 @@ def _q4_k_values(qs: np.ndarray) -> np.ndarray:
 def _q5_k_values(qh: np.ndarray, qs: np.ndarray) -> np.ndarray:
     """Q4_K nibbles plus a fifth bit: sub-block k takes bit k of qh[j] for value j.
     ``ggml_quant.py:311-349`` (bit 2n for low nibbles, 2n+1 for high nibbles of group n)."""
-    vals = _q4_k_values(qs).view(np.uint8).copy()
-    for k in range(8):
-        vals[:, k, :] |= ((qh >> k) & 1) << 4
-    return vals.view(np.int8)
+    fifth = ((qh[:, None, :] >> np.arange(8, dtype=np.uint8)[None, :, None]) & 1) << 4
+    return (_q4_k_values(qs).view(np.uint8) | fifth).view(np.int8)
 
 
-def _q6_k_values(ql: np.ndarray, qh: np.ndarray) -> np.ndarray:
+def _q6_k_values(ql: np.ndarray, qh: np.ndarray, chunk: int = 4096) -> np.ndarray:
     """Q6_K: value 128h + 32g + j of a super-block is (nibble | 2 high bits << 4) - 32,
     where the nibble is the low (g<2) or high (g>=2) nibble of ql[64h + 32(g&1) + j] and
-    the high bits are bits 2g..2g+1 of qh[32h + j].  ``ggml_quant.py:274-308``."""
+    the high bits are bits 2g..2g+1 of qh[32h + j].  ``ggml_quant.py:274-308``.  Built
+    `chunk` super-blocks at a time, so the temporaries stay in cache."""
     n = ql.shape[0]
     out = np.empty((n, 2, 4, 32), dtype=np.uint8)
-    for h in range(2):
-        hb = qh[:, 32 * h:32 * h + 32]
-        for g in range(4):
-            src = ql[:, 64 * h + 32 * (g & 1):64 * h + 32 * (g & 1) + 32]
-            nib = (src & 0x0F) if g < 2 else (src >> 4)
-            out[:, h, g, :] = nib | (((hb >> (2 * g)) & 3) << 4)
-    return (out.view(np.int8) - np.int8(32)).reshape(n, 16, 16)
+    shifts = np.array([0, 2, 4, 6], dtype=np.uint8).reshape(1, 1, 4, 1)
+    for a in range(0, n, chunk):
+        b = min(n, a + chunk)
+        q = ql[a:b].reshape(b - a, 2, 2, 32)                     # [h, g & 1, j]
+        hb = ((qh[a:b].reshape(b - a, 2, 1, 32) >> shifts) & 3) << 4
+        o = out[a:b]
+        np.bitwise_or(q & 0x0F, hb[:, :, 0:2], out=o[:, :, 0:2])
+        np.bitwise_or(q >> 4, hb[:, :, 2:4], out=o[:, :, 2:4])
+    v = out.view(np.int8)
+    v -= np.int8(32)
+    return v.reshape(n, 16, 16)
 
 
 def _q2_k_values(qs: np.ndarray) -> np.ndarray:
@@ -274,15 +279,6 @@ def remove_superblocks(sup: np.ndarray, blk: np.ndarray, vals: np.ndarray):
     return bc.reshape(n_blocks, bc.shape[2]), vals.reshape(n_blocks, vals.shape[2])
 
 
-def _i16_cast(x: np.ndarray) -> np.ndarray:
-    """float32 -> int16 as numpy does it on x86-64: through int32, where NaN and values
-    outside int32 give INT32_MIN, then keep the low 16 bits."""
-    x = np.asarray(x, dtype=np.float32)
-    ok = np.abs(x) < np.float32(2147483648.0)
-    i32 = np.where(ok, np.trunc(np.where(ok, x, 0)), 0).astype(np.int64).astype(np.int32)
-    return i32.astype(np.int16)
-
-
 @dataclass
 class RequantDiag:
     round_error: np.float32
@@ -310,21 +306,23 @@ def requantize_symmetric(bc: np.ndarray, q: np.ndarray, output_bits: int = 8,
     M = bc[:, 1]
     S_eff = np.where(S == 0, np.where(np.abs(M) > SCALE_EPSILON, M, SCALE_EPSILON), S).astype(np.float32)
     with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
-        r = (M / S_eff).astype(np.float32)
-        lo = (q.min(axis=1).astype(np.float32) + r).astype(np.float32)
-        hi = (q.max(axis=1).astype(np.float32) + r).astype(np.float32)
-        sf = np.full(S.shape, np.float32(16))
-        sf = np.minimum(sf, np.where(lo < 0, np.float32(lo_out) / lo, np.float32(16)).astype(np.float32))
-        sf = np.minimum(sf, np.where(hi > 0, np.float32(hi_out) / hi, np.float32(16)).astype(np.float32))
-        sf = np.where(sf > np.float32(0.98), np.maximum(np.floor(sf), np.float32(1)), sf).astype(np.float32)
-        rmv = (r * sf).astype(np.float32)
-        rm = _i16_cast(np.rint(rmv))
-        round_error = np.max(np.abs(rm.astype(np.float32) - rmv))
-        scaled = _i16_cast(np.rint(q.astype(np.float32) * sf[:, None]))
-        unclipped = (scaled + rm[:, None]).astype(np.int16)
-        clipped = np.clip(unclipped, lo_out, hi_out).astype(np.int16)
+        r = M / S_eff
+        lo = q.min(axis=1) + r
+        hi = q.max(axis=1) + r
+        sf = np.minimum(np.float32(16), np.where(lo < 0, np.float32(lo_out) / lo, np.float32(16)))
+        np.minimum(sf, np.where(hi > 0, np.float32(hi_out) / hi, np.float32(16)), out=sf)
+        sf = np.where(sf > np.float32(0.98), np.maximum(np.floor(sf), np.float32(1)), sf)
+        rmv = r * sf
+        # float32 -> int16 by numpy's own cast, as the reference does it (on x86-64 through
+        # int32: NaN and out-of-range values give INT32_MIN, whose low 16 bits are 0)
+        rm = np.rint(rmv).astype(np.int16)
+        round_error = np.max(np.abs(rm - rmv))
+        unclipped = np.rint(q * sf[:, None]).astype(np.int16)
+        unclipped += rm[:, None]
+        clipped = np.clip(unclipped, lo_out, hi_out)
         clip_error = np.max(np.abs(clipped - unclipped))
-        scales = (S / sf).astype(np.float32).reshape(-1, 1)
+        scales = (S / sf).reshape(-1, 1)
+    assert scales.dtype == np.float32 and sf.dtype == np.float32
     if log and (clip_error > 0 or round_error > 0.5):
         _log.warning(f"Distortion from requantization: rounding {round_error}, clipping {clip_error}")
     return scales, clipped.astype(new_dtype), RequantDiag(np.float32(round_error), np.int16(clip_error))
