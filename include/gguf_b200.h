@@ -247,6 +247,21 @@ GQ_API int gq_session_destroy(gq_session_t* session);
 GQ_API int gq_convert_host(gq_session_t* session, const gq_tensor_t* tensors, int32_t count,
                     int32_t out_mask, gq_diag_t* host_diags);
 
+/* Page-locked host buffers for conversion results, recycled.  No counterpart in the
+ * reference, whose calls return fresh numpy arrays (gguf_conversion.py:279-300).  A result
+ * buffer in page-locked memory is written by the copy engines directly, where a fresh
+ * pageable one costs page zeroing on first touch and a host copy out of a bounce slot;
+ * gq_host_free keeps the buffer for the next request of its size class (classes of 2^k
+ * and 1.5 * 2^k bytes, at least 64 KiB), so a caller converting one tensor at a time pins
+ * memory once per class.  In use plus kept buffers stay under a limit (environment
+ * LLIMA_B200_PINNED_RESULTS_MB; default a quarter of host memory, at most 16 GiB): past it
+ * gq_host_alloc fails with GQ_ERR_NOMEM and the caller uses ordinary memory.  Kept buffers
+ * of other classes are released first to make room; gq_host_trim releases all kept ones.
+ * Thread-safe; a forked child starts with an empty arena. */
+GQ_API int gq_host_alloc(size_t bytes, void** out);
+GQ_API int gq_host_free(void* ptr);
+GQ_API int gq_host_trim(void);
+
 /* Allocation-free host-buffer conversion.  No counterpart in the reference: it exists for
  * callers that must not allocate device memory while they prepare weights, e.g. a process
  * whose device memory already belongs to another allocator (a framework's caching pool or

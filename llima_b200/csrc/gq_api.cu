@@ -9,6 +9,8 @@
 #include <atomic>
 #include <cerrno>
 #include <deque>
+#include <map>
+#include <unordered_map>
 #include <condition_variable>
 #include <cstdlib>
 #include <cstring>
@@ -476,6 +478,127 @@ int gq_quantize_rows(const float* x, int64_t rows, int64_t cols, int8_t* codes, 
     return cuda_status(gq::launch_embed(GQ_TYPE_F32, true, reinterpret_cast<const uint8_t*>(x), rows, cols, cols * 4,
                                         1.0f, 1, codes, scales_bf16, nullptr, rows * cols * 4, stream));
 }
+
+// ---------------------------------------------------------------------------------------
+// Page-locked result buffers, recycled
+//
+// The drop-in call returns a fresh array per tensor.  A fresh pageable array costs the
+// kernel's page zeroing on first touch and a host copy out of a pinned bounce slot; a
+// page-locked one is written by the copy engines directly.  Buffers are handed out in size
+// classes (two per octave) and a released buffer waits for the next request of its class,
+// so a caller that converts one tensor at a time pays for pinning once per class.
+// ---------------------------------------------------------------------------------------
+
+namespace {
+
+struct HostArena {
+    std::mutex mu;
+    pid_t pid = 0;
+    size_t limit = 0;      // in use + cached, bytes
+    size_t in_use = 0;
+    size_t cached = 0;
+    std::map<size_t, std::vector<void*>> free_by_class;
+    std::unordered_map<void*, size_t> owned;   // every block of this process -> class size
+
+    void init_locked() {
+        if (pid == getpid()) return;
+        // a forked child owns none of its parent's page-locked blocks
+        pid = getpid();
+        in_use = cached = 0;
+        free_by_class.clear();
+        owned.clear();
+        long mb = -1;
+        if (const char* e = std::getenv("LLIMA_B200_PINNED_RESULTS_MB")) mb = std::atol(e);
+        if (mb >= 0) {
+            limit = static_cast<size_t>(mb) << 20;
+        } else {
+            const long pages = sysconf(_SC_PHYS_PAGES), page = sysconf(_SC_PAGE_SIZE);
+            const size_t phys = (pages > 0 && page > 0) ? static_cast<size_t>(pages) * static_cast<size_t>(page) : 0;
+            limit = std::min<size_t>(phys / 4, size_t(16) << 30);
+        }
+    }
+};
+HostArena g_arena;
+
+// Smallest size class >= bytes: 2^k or 3 * 2^(k-1), at least 64 KiB.
+size_t size_class(size_t bytes) {
+    size_t c = size_t(64) << 10;
+    while (c < bytes) {
+        const size_t mid = c + c / 2;
+        if (mid >= bytes) return mid;
+        c *= 2;
+    }
+    return c;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gq_host_alloc(size_t bytes, void** out) {
+    if (out == nullptr) return GQ_ERR_NULL;
+    *out = nullptr;
+    if (bytes == 0) return GQ_ERR_ARG;
+    const size_t cls = size_class(bytes);
+    std::lock_guard<std::mutex> lock(g_arena.mu);
+    g_arena.init_locked();
+    auto it = g_arena.free_by_class.find(cls);
+    if (it != g_arena.free_by_class.end() && !it->second.empty()) {
+        *out = it->second.back();
+        it->second.pop_back();
+        g_arena.cached -= cls;
+        g_arena.in_use += cls;
+        return GQ_OK;
+    }
+    // make room: release cached blocks of other classes first
+    while (g_arena.in_use + g_arena.cached + cls > g_arena.limit && g_arena.cached > 0) {
+        auto big = std::prev(g_arena.free_by_class.end());
+        while (big->second.empty()) big = std::prev(big);
+        cudaFreeHost(big->second.back());
+        g_arena.owned.erase(big->second.back());
+        big->second.pop_back();
+        g_arena.cached -= big->first;
+    }
+    if (g_arena.in_use + cls > g_arena.limit) return GQ_ERR_NOMEM;
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, cls, cudaHostAllocPortable) != cudaSuccess) {
+        cudaGetLastError();
+        return GQ_ERR_NOMEM;
+    }
+    g_arena.owned[p] = cls;
+    g_arena.in_use += cls;
+    *out = p;
+    return GQ_OK;
+}
+
+int gq_host_free(void* p) {
+    if (p == nullptr) return GQ_OK;
+    std::lock_guard<std::mutex> lock(g_arena.mu);
+    if (g_arena.pid != getpid()) return GQ_ERR_ARG;   // not from this process's arena
+    auto it = g_arena.owned.find(p);
+    if (it == g_arena.owned.end()) return GQ_ERR_ARG;
+    const size_t cls = it->second;
+    g_arena.in_use -= cls;
+    g_arena.free_by_class[cls].push_back(p);
+    g_arena.cached += cls;
+    return GQ_OK;
+}
+
+int gq_host_trim(void) {
+    std::lock_guard<std::mutex> lock(g_arena.mu);
+    if (g_arena.pid != getpid()) return GQ_OK;
+    for (auto& kv : g_arena.free_by_class) {
+        for (void* p : kv.second) {
+            cudaFreeHost(p);
+            g_arena.owned.erase(p);
+        }
+        kv.second.clear();
+    }
+    g_arena.cached = 0;
+    return GQ_OK;
+}
+
+}  // extern "C"
 
 // ---------------------------------------------------------------------------------------
 // Host-buffer session

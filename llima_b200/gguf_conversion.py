@@ -21,6 +21,7 @@ import logging
 import mmap
 import os
 import threading
+import weakref
 from pathlib import Path
 
 import numpy as np
@@ -80,13 +81,55 @@ def _host_ptr(a: np.ndarray) -> int:
 _HUGE_MIN = 8 << 20
 
 
+_PINNED_MIN = 1 << 20
+
+
+class _PinnedBlock:
+    """Owner of one page-locked buffer from the library's result arena (gq_host_alloc): the
+    arrays viewing it keep it alive, and the buffer goes back to the arena for the next
+    result of its size once the last of them is gone."""
+    __slots__ = ("ptr", "nbytes", "__weakref__")
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.ptr = ptr
+        self.nbytes = nbytes
+        weakref.finalize(self, _pinned_release, ptr).atexit = False
+
+    @property
+    def __array_interface__(self):
+        # numpy keeps the object that exports the buffer as the array's base
+        return {"shape": (self.nbytes,), "typestr": "|u1", "data": (self.ptr, False), "version": 3}
+
+
+def _pinned_release(ptr: int) -> None:
+    try:
+        N.lib().gq_host_free(ptr)
+    except Exception:   # interpreter shutdown: the process frees everything anyway
+        pass
+
+
+def _pinned_empty(shape, dtype: np.dtype, n: int):
+    """A result array in a recycled page-locked buffer, or None when the arena is full or
+    turned off (LLIMA_B200_PINNED_RESULTS_MB=0)."""
+    ptr = ctypes.c_void_p()
+    if N.lib().gq_host_alloc(n, ctypes.byref(ptr)) != N.GQ_OK or not ptr.value:
+        return None
+    return np.asarray(_PinnedBlock(ptr.value, n)).view(dtype).reshape(shape)
+
+
 def _host_empty(shape, dtype) -> np.ndarray:
-    """An uninitialised host array for a conversion result.  Large ones are backed by an
-    anonymous mapping with transparent huge pages requested, so that the first writes
-    (by the library's copy threads) fault in 2 MiB pages instead of 4 KiB ones; the
-    array owns the mapping and frees it with itself."""
+    """An uninitialised host array for a conversion result.  From 1 MiB on it lives in a
+    page-locked buffer of the library's recycled result arena, which the copy engines write
+    directly (no page faults, no host copy); when the arena is full, large arrays are
+    backed by an anonymous mapping with transparent huge pages requested, so that the first
+    writes (by the library's copy threads) fault in 2 MiB pages instead of 4 KiB ones; the
+    array owns its memory and frees it (or returns it to the arena) with itself."""
     dtype = np.dtype(dtype)
     n = int(np.prod(shape)) * dtype.itemsize
+    if n >= _PINNED_MIN:
+        arr = _pinned_empty(shape, dtype, n)
+        if arr is not None:
+            return arr
     if n < _HUGE_MIN:
         return np.empty(shape, dtype=dtype)
     m = mmap.mmap(-1, n, flags=mmap.MAP_PRIVATE | mmap.MAP_ANONYMOUS)
