@@ -294,27 +294,36 @@ def workload_config(args, world) -> dict:
             "l2": "inputs larger than L2 (GGUF bytes >> 126 MB), no flush"}
 
 
-def gguf_file_e2e(tensors, host_src, layers: int = 8):
-    """GB/s of convert_gguf_file on a real GGUF file: the embedding, the output head and
-    the first `layers` layers of the rank's tensors written with gguf-py's writer to a
-    scratch file (page-cached; /dev/shm when it has room), converted once to warm the page
-    cache and the session, then timed once.  None when there is no room for the file."""
+def gguf_file_e2e(tensors, host_src, layers: int | None = None):
+    """The host-to-host paths a user of the reference's loader takes, on a real GGUF file:
+    the rank's tensors (all of them, or the embedding, the output head and the first
+    `layers` layers) written with gguf-py's writer to a scratch file (page-cached; /dev/shm
+    when it has room).  Returns two records, or (None, None) when there is no room:
+
+    * from_gguf_file: convert_gguf_file, every quantized tensor in one host call (warmed up
+      once, then timed once on a fresh reader);
+    * dropin: GgufModel.load_weight's path, one load_tensor call per quantized tensor on a
+      fresh GGUFReader (its memory map is page-locked by the first call, inside the timed
+      loop), each result dropped before the next call."""
     import shutil
     import numpy as np
     import gguf
-    from llima_b200.gguf_conversion import convert_gguf_file
+    from llima_b200.gguf_conversion import convert_gguf_file, load_tensor
     keep = [(t, hs) for t, hs in zip(tensors, host_src)
-            if not t.name.startswith("blk.") or int(t.name.split(".")[1]) < layers]
+            if layers is None or not t.name.startswith("blk.") or int(t.name.split(".")[1]) < layers]
     total = sum(hs.numel() for _, hs in keep)
-    d = "/dev/shm" if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > 3 * total \
+    need = int(1.2 * total) + (1 << 30)
+    d = "/dev/shm" if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > need \
         else tempfile.gettempdir()
-    if shutil.disk_usage(d).free < 3 * total:
-        return None
+    if shutil.disk_usage(d).free < need:
+        return None, None
     path = os.path.join(d, f"llima_b200_bench_{os.getpid()}.gguf")
+    cut = "whole model" if layers is None else f"embedding, output and the first {layers} layers"
     try:
         w = gguf.GGUFWriter(path, "llama")
         heads = {t.name.split(".")[-2]: t.perm_heads for t, _ in keep if t.perm_heads}
-        w.add_block_count(layers)
+        n_layers = 1 + max([int(t.name.split(".")[1]) for t, _ in keep if t.name.startswith("blk.")] or [0])
+        w.add_block_count(n_layers)
         if "attn_q" in heads:
             w.add_head_count(heads["attn_q"])
             w.add_head_count_kv(heads.get("attn_k", heads["attn_q"]))
@@ -338,9 +347,24 @@ def gguf_file_e2e(tensors, host_src, layers: int = 8):
         dt = time.perf_counter() - t0
         n = len(res)
         del res
-        return {"value": round(total / dt / 1e9, 3), "unit": "GB/s", "seconds": round(dt, 4), "gguf_bytes": total,
-                "tensors": n, "cut": f"embedding, output and the first {layers} layers",
-                "api": "convert_gguf_file (GGUFReader memory map, one gq_convert_host call)"}
+        whole = {"value": round(total / dt / 1e9, 3), "unit": "GB/s", "seconds": round(dt, 4), "gguf_bytes": total,
+                 "tensors": n, "cut": cut,
+                 "api": "convert_gguf_file (GGUFReader memory map, one gq_convert_host call)"}
+        perm = {t.name: t.perm_heads for t, _ in keep}
+        reader = gguf.GGUFReader(path)
+        quant = [rt for rt in reader.tensors if rt.tensor_type.name not in ("F32", "F16", "BF16")]
+        qbytes = sum(int(rt.n_bytes) for rt in quant)
+        t0 = time.perf_counter()
+        for rt in quant:
+            s_, w_ = load_tensor(rt, False, perm.get(rt.name, 0))
+            del s_, w_
+        dt = time.perf_counter() - t0
+        del quant, reader
+        dropin = {"value": round(qbytes / dt / 1e9, 3), "unit": "GB/s", "s_per_model": round(dt, 4),
+                  "gguf_bytes": qbytes, "tensors": len(perm), "cut": cut,
+                  "api": "gguf_conversion.load_tensor, one call per quantized tensor of a GGUFReader "
+                         "(GgufModel.load_weight's path): memory-mapped file in, numpy arrays out"}
+        return whole, dropin
     finally:
         if os.path.exists(path):
             os.unlink(path)
@@ -776,7 +800,7 @@ def run_ours(args, rank, world, local_rank):
         dropin_bytes = float(sum(r.size for _, r in quant))
         del quant
         # from a GGUF file on one GPU (ranks of a multi-GPU run would each need their own)
-        file_e2e = gguf_file_e2e(tensors, host_src) if world == 1 else None
+        file_e2e, file_dropin = gguf_file_e2e(tensors, host_src) if world == 1 else (None, None)
         h2d = sum(h.numel() for h in host_src)
         d2h = sum(ht.numel() * ht.element_size() for outs in host_out for ht in outs.values())
         agg = torch.tensor([float(gguf_bytes), float(h2d), float(d2h), 1.0 if same else 0.0, dropin_bytes],
@@ -788,10 +812,11 @@ def run_ours(args, rank, world, local_rank):
         e2e = {"value": float(agg[0].item()) / e2e_s / 1e9, "unit": "GB/s", "s_per_model": e2e_s,
                "h2d_bytes_per_step": int(agg[1].item()), "d2h_bytes_per_step": int(agg[2].item()),
                "matches_device": bool(agg[3].item() == world), "api": "gq_convert_host (pinned host buffers)",
-               "dropin_pageable": {"value": round(float(agg[4].item()) / float(tmax.item()) / 1e9, 3), "unit": "GB/s",
-                                   "s_per_model": round(float(tmax.item()), 4),
-                                   "api": "gguf_conversion.convert_host, one call per tensor, pageable numpy "
-                                          "in/out (GgufModel.load_weight's path)"},
+               "dropin_pageable": file_dropin,
+               "dropin_numpy_copies": {"value": round(float(agg[4].item()) / float(tmax.item()) / 1e9, 3),
+                                       "unit": "GB/s", "s_per_model": round(float(tmax.item()), 4),
+                                       "api": "gguf_conversion.convert_host, one call per tensor, pageable numpy "
+                                              "arrays in (not a memory map: bounced), numpy arrays out"},
                "from_gguf_file": file_e2e}
         del host_src, host_out
 

@@ -584,6 +584,31 @@ int gq_host_free(void* p) {
     return GQ_OK;
 }
 
+int gq_host_register(const void* ptr, size_t bytes, int32_t read_only) {
+    if (ptr == nullptr) return GQ_ERR_NULL;
+    if (bytes == 0) return GQ_ERR_ARG;
+    const uintptr_t page = static_cast<uintptr_t>(sysconf(_SC_PAGE_SIZE));
+    const uintptr_t a = reinterpret_cast<uintptr_t>(ptr) & ~(page - 1);
+    const uintptr_t b = (reinterpret_cast<uintptr_t>(ptr) + bytes + page - 1) & ~(page - 1);
+    unsigned flags = cudaHostRegisterPortable;
+    if (read_only != 0) {
+        int dev = 0, ok = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&ok, cudaDevAttrHostRegisterReadOnlySupported, dev) != cudaSuccess || !ok) {
+            cudaGetLastError();
+            return GQ_ERR_ARG;
+        }
+        flags |= cudaHostRegisterReadOnly;
+    }
+    return cuda_status(cudaHostRegister(reinterpret_cast<void*>(a), b - a, flags));
+}
+
+int gq_host_unregister(const void* ptr) {
+    if (ptr == nullptr) return GQ_ERR_NULL;
+    const uintptr_t page = static_cast<uintptr_t>(sysconf(_SC_PAGE_SIZE));
+    return cuda_status(cudaHostUnregister(reinterpret_cast<void*>(reinterpret_cast<uintptr_t>(ptr) & ~(page - 1))));
+}
+
 int gq_host_trim(void) {
     std::lock_guard<std::mutex> lock(g_arena.mu);
     if (g_arena.pid != getpid()) return GQ_OK;
