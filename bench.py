@@ -303,8 +303,8 @@ def gguf_file_e2e(tensors, host_src, layers: int | None = None):
     * from_gguf_file: convert_gguf_file, every quantized tensor in one host call (warmed up
       once, then timed once on a fresh reader);
     * dropin: GgufModel.load_weight's path, one load_tensor call per quantized tensor on a
-      fresh GGUFReader (its memory map is page-locked by the first call, inside the timed
-      loop), each result dropped before the next call."""
+      fresh GGUFReader (its memory map's pages are read inside the timed loop), each result
+      dropped before the next call."""
     import shutil
     import numpy as np
     import gguf

@@ -262,16 +262,6 @@ GQ_API int gq_host_alloc(size_t bytes, void** out);
 GQ_API int gq_host_free(void* ptr);
 GQ_API int gq_host_trim(void);
 
-/* Page-locks host memory that conversion inputs are read from, typically the whole memory
- * map of a GGUF file, so that gq_convert_host copies tensors out of it with the copy
- * engines directly instead of bouncing them through its pinned slots.  The range is
- * rounded out to whole pages, which must belong to the caller; read_only != 0 for a
- * mapping without write access (needs the device's read-only registration support, else
- * GQ_ERR_ARG).  gq_host_unregister takes the same ptr; unregister before unmapping.  No
- * counterpart in the reference. */
-GQ_API int gq_host_register(const void* ptr, size_t bytes, int32_t read_only);
-GQ_API int gq_host_unregister(const void* ptr);
-
 /* Allocation-free host-buffer conversion.  No counterpart in the reference: it exists for
  * callers that must not allocate device memory while they prepare weights, e.g. a process
  * whose device memory already belongs to another allocator (a framework's caching pool or

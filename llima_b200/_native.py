@@ -24,7 +24,7 @@ EXPORTS = ("gq_version", "gq_strerror", "gq_last_cuda_error", "gq_kernel_errors"
            "gq_session_destroy", "gq_convert_host", "gq_convert_host_noalloc", "gq_embedding_rows",
            "gq_quantize_rows", "gq_modalix_layout", "gq_unpack_fields", "gq_remove_superblocks",
            "gq_convert_modalix", "gq_convert_modalix_batch",
-           "gq_host_alloc", "gq_host_free", "gq_host_trim", "gq_host_register", "gq_host_unregister")
+           "gq_host_alloc", "gq_host_free", "gq_host_trim")
 
 
 class NativeLibraryError(RuntimeError):
@@ -77,8 +77,6 @@ def _declare(lib):
         "gq_host_alloc": ([SZ, ctypes.POINTER(P)], ctypes.c_int),
         "gq_host_free": ([P], ctypes.c_int),
         "gq_host_trim": ([], ctypes.c_int),
-        "gq_host_register": ([P, SZ, I32], ctypes.c_int),
-        "gq_host_unregister": ([P], ctypes.c_int),
         "gq_query": ([I32, I64, I64, ctypes.POINTER(Layout)], ctypes.c_int),
         "gq_diag_reset": ([P, I32, P], ctypes.c_int),
         "gq_convert": ([ctypes.POINTER(Tensor), I32, P], ctypes.c_int),

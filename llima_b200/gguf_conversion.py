@@ -117,50 +117,6 @@ def _pinned_empty(shape, dtype: np.dtype, n: int):
     return np.asarray(_PinnedBlock(ptr.value, n)).view(dtype).reshape(shape)
 
 
-_mapped: dict[tuple[int, int], object] = {}
-_mapped_lock = threading.Lock()
-
-
-def _unregister_mapping(key) -> None:
-    with _mapped_lock:
-        _mapped.pop(key, None)
-    try:
-        N.lib().gq_host_unregister(key[1])
-    except Exception:   # interpreter shutdown
-        pass
-
-
-def _register_source(a) -> None:
-    """Page-lock, once per process, the memory map a tensor's GGUF bytes are a view of (the
-    GGUFReader's np.memmap of the file), so that the library copies every tensor out of it
-    directly instead of through its bounce slots.  The registration ends when the map's
-    array is collected, before the map itself is released.  Nothing happens for bytes that
-    do not come from a memory map, or when the driver refuses (they are bounced as before);
-    LLIMA_B200_REGISTER_MAPS=0 turns it off."""
-    if os.environ.get("LLIMA_B200_REGISTER_MAPS", "1") == "0":
-        return
-    root, b = None, a
-    while b is not None:
-        if isinstance(b, mmap.mmap):
-            break
-        if isinstance(b, np.ndarray):
-            root = b
-        b = getattr(b, "base", None)
-    if b is None or root is None or root.nbytes == 0:
-        return
-    key = (os.getpid(), root.ctypes.data)
-    with _mapped_lock:
-        if key in _mapped:
-            return
-        st = N.lib().gq_host_register(root.ctypes.data, root.nbytes, 0 if root.flags.writeable else 1)
-        if st != N.GQ_OK:
-            _mapped[key] = None   # refused: do not retry for this map
-            return
-        fin = weakref.finalize(root, _unregister_mapping, key)
-        fin.atexit = False
-        _mapped[key] = fin
-
-
 def _host_empty(shape, dtype) -> np.ndarray:
     """An uninitialised host array for a conversion result.  From 1 MiB on it lives in a
     page-locked buffer of the library's recycled result arena, which the copy engines write
@@ -290,7 +246,6 @@ def convert_gguf_file(path, names=None, force_float: bool = False, permute_qk: b
         cols = int(np.prod(shape[1:])) if len(shape) > 1 else 1
         if f.asymmetric and not force_float and rows * cols == 0:
             raise ValueError("zero-size array to reduction operation maximum which has no identity")
-        _register_source(t.data)
         raw = np.ascontiguousarray(np.asarray(t.data)).reshape(-1).view(np.uint8)
         r = N.Tensor()
         r.type, r.perm_heads, r.rows, r.cols = f.type_id, heads, rows, cols
@@ -352,7 +307,6 @@ def load_tensor(gguf_tensor, force_float: bool, perm_heads: int = 0):
         raise NotImplementedError(f"GGML type {name} is not handled by the B200 GGUF path")
     rows = shape[0]
     cols = int(np.prod(shape[1:])) if len(shape) > 1 else 1
-    _register_source(gguf_tensor.data)
     s, w, d = convert_host(name, np.asarray(gguf_tensor.data), rows, cols, force_float, perm_heads)
     if d is not None:
         requant_warning(*d)
@@ -386,7 +340,6 @@ def load_partition(gguf_tensor, count: int, index: int, span: int, force_float: 
     cols = int(np.prod(shape[1:])) if len(shape) > 1 else 1
     row_bytes = cols // f.unit_values * f.unit_bytes
     raw = np.asarray(gguf_tensor.data).reshape(-1).view(np.uint8)[r0 * row_bytes:r1 * row_bytes]
-    _register_source(gguf_tensor.data)
     s, w, d = convert_host(name, raw, r1 - r0, cols, force_float)
     if d is not None:
         requant_warning(*d)

@@ -84,34 +84,3 @@ def test_arena_limits_and_fallback():
     _, codes, _ = G.convert_host("Q4_K", raw, 256, 4096)
     assert np.array_equal(np.load(out), codes)
     out.unlink()
-
-
-def test_gguf_memory_map_is_registered_once_and_released(tmp_path):
-    import gc
-    gguf = pytest.importorskip("gguf")
-    path = tmp_path / "m.gguf"
-    w = gguf.GGUFWriter(str(path), "llama")
-    raws = {}
-    for i, (fmt, rows, cols) in enumerate([("Q4_K", 256, 1024), ("Q6_K", 128, 2048), ("Q8_0", 64, 512)]):
-        raw = gen_tensor_bytes(fmt, rows * cols, 300 + i)
-        raws[f"t{i}"] = (fmt, rows, cols, raw)
-        w.add_tensor(f"t{i}", raw.reshape(rows, -1), raw_shape=(rows, raw.size // rows),
-                     raw_dtype=getattr(gguf.GGMLQuantizationType, fmt))
-    w.write_header_to_file()
-    w.write_kv_data_to_file()
-    w.write_tensors_to_file()
-    w.close()
-    reader = gguf.GGUFReader(str(path))
-    before = set(G._mapped)
-    for t in reader.tensors:
-        fmt, rows, cols, raw = raws[t.name]
-        s, c = G.load_tensor(t, False)
-        with np.errstate(all="ignore"):
-            s_ref, w_ref, _ = O.unpack_tensor(fmt, raw.tobytes(), (rows, cols), log=False)
-        assert np.array_equal(c.view(np.uint8), w_ref.view(np.uint8))
-        assert np.array_equal(s.view(np.uint32), s_ref.view(np.uint32))
-    added = set(G._mapped) - before
-    assert len(added) == 1 and G._mapped[next(iter(added))] is not None   # one map, registered
-    del reader, t, s, c
-    gc.collect()
-    assert not (set(G._mapped) & added)                                     # released with the map
