@@ -52,6 +52,10 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0,
                     help="keep only the first L transformer layers (small cases for profiling)")
     ap.add_argument("--formats", default="", help="comma list of GGML formats to keep (profiling)")
+    ap.add_argument("--tensor", default="",
+                    help="FMT:ROWS:COLS: instead of a model set, --copies seeded copies of one tensor "
+                         "(a BASELINE single-tensor config), all converted by one launch per step")
+    ap.add_argument("--copies", type=int, default=8)
     ap.add_argument("--no-sustained", action="store_true", help="skip the >= 1 s steady-state timing")
     ap.add_argument("--sustained-seconds", type=float, default=1.5)
     ap.add_argument("--no-configs", action="store_true",
@@ -61,8 +65,13 @@ def parse_args():
 
 
 def selected_specs(args):
-    """The model's tensor list, optionally cut to the first --layers layers / --formats."""
-    from llima_b200.synth import model_specs
+    """The model's tensor list, optionally cut to the first --layers layers / --formats, or
+    --copies copies of the single --tensor."""
+    from llima_b200.synth import TensorSpec, model_specs
+    if args.tensor:
+        fmt, rows, cols = args.tensor.split(":")
+        return [TensorSpec(f"{fmt}_{rows}x{cols}.{i}", fmt, int(rows), int(cols), 9000 + i)
+                for i in range(args.copies)]
     specs = model_specs(args.model, args.seed)
     if args.layers:
         keep = []
@@ -288,7 +297,10 @@ def workload_config(args, world) -> dict:
     cut = ""
     if args.layers or args.formats:
         cut = f" (cut: layers={args.layers or 'all'}, formats={args.formats or 'all'})"
-    return {"workload": f"{args.model} GGUF tensor set, whole model per step{cut}", "model": args.model,
+    workload = f"{args.model} GGUF tensor set, whole model per step{cut}"
+    if args.tensor:
+        workload = f"{args.copies} seeded copies of one {args.tensor} tensor, one launch per step"
+    return {"workload": workload, "model": args.model if not args.tensor else args.tensor,
             "n_tensors": len(specs), "gguf_bytes": gguf, "out_bytes": out, "output": args.out,
             "parallelism": f"tensor-shard x{world}",
             "l2": "inputs larger than L2 (GGUF bytes >> 126 MB), no flush"}
@@ -823,7 +835,7 @@ def run_ours(args, rank, world, local_rank):
     # ---- the other BASELINE workloads, each after the previous one's memory is freed
     del tensors, batches
     ds.free()
-    full_set = not (args.layers or args.formats) and out_mask == N.OUT_CODES
+    full_set = not (args.layers or args.formats or args.tensor) and out_mask == N.OUT_CODES
     peak_, _ = measured_peak()
     configs = None
     if not args.no_configs and out_mask == N.OUT_CODES:
