@@ -18,6 +18,10 @@
 // The fp32 intermediate of dequant -> requant never touches global memory.
 #include <cuda_runtime.h>
 
+#include <memory>
+#include <new>
+#include <type_traits>
+
 #include "gq_device.cuh"
 #include "gq_internal.h"
 
@@ -29,13 +33,15 @@ namespace gq {
 
 // Sub-tiles of 8 super-blocks per Q4_K / Q5_K loop iteration, processed one after the
 // other (the per-tile bookkeeping is shared, the registers are not multiplied), and the
-// pipeline depth.  Measured on B200 (8-layer Llama-3-8B Q4_K set): 1 sub-tile x 4 stages
-// at 3 CTAs/SM 2.99 TB/s, 4 sub-tiles x 3 stages at 2 CTAs/SM 3.23 TB/s.
+// pipeline depth.  With one bulk copy per tile, fewer and larger tiles win (8-layer cuts,
+// fraction of the measured copy peak, Q4_K / Q5_K): 6 (Q5_K 5) sub-tiles x 2 stages
+// 0.795 / 0.749, 4 x 3 (Q5_K 4 x 2) 0.786 / 0.743, 3 x 4 0.768 / 0.725, 2 x 6 0.737 / 0.697,
+// 4 x 4 at 6-warp CTAs 0.698 / 0.667.
 #ifndef GQ_K45_SUB
-#define GQ_K45_SUB 4
+#define GQ_K45_SUB 6
 #endif
 #ifndef GQ_K45_STAGES
-#define GQ_K45_STAGES 3
+#define GQ_K45_STAGES 2
 #endif
 #ifndef GQ_K45_WARPS
 #define GQ_K45_WARPS 8
@@ -46,10 +52,10 @@ namespace gq {
 #ifndef GQ_Q6K_STAGES
 #define GQ_Q6K_STAGES 3
 #endif
-// Q5_K, measured on B200 (8-layer Qwen2.5-7B Q5_K set, GB/s): 1 sub-tile x 4 stages 3930,
-// 2 x 3 4240, 3 x 3 4387, 4 x 2 4484-4493, 5 x 2 4487, 4 x 3 at 6 warps 4052.
+// Q5_K with per-lane copies (8-layer Qwen2.5-7B Q5_K set, GB/s): 1 sub-tile x 4 stages
+// 3930, 2 x 3 4240, 3 x 3 4387, 4 x 2 4484-4493, 5 x 2 4487, 4 x 3 at 6 warps 4052.
 #ifndef GQ_Q5K_SUB
-#define GQ_Q5K_SUB 4
+#define GQ_Q5K_SUB 5
 #endif
 #ifndef GQ_Q5K_STAGES
 #define GQ_Q5K_STAGES 2
@@ -94,6 +100,18 @@ GQ_FMT(GQ_TYPE_Q5_1, 24, 32, 4, 8, GQ_Q0_BULK)
 GQ_FMT(GQ_TYPE_Q2_K, 84, 8, 4, 8, GQ_Q0_BULK)    // 128 blocks of 16 per tile, one per lane and round
 GQ_FMT(GQ_TYPE_Q3_K, 110, 8, 4, 8, GQ_Q0_BULK)
 #undef GQ_FMT
+
+// Q4_K / Q5_K launches with few tiles per warp (one tensor of a BASELINE single-tensor
+// config, a host call's piece) use 4 sub-tiles per tile instead (Q4_K with 3 stages): the
+// C2 Q4_K 11008x4096 tensor alone measured 0.585 of the copy peak so against 0.485 in the
+// big tiles, and 0.559 with 1 sub-tile x 6 stages.
+template <int TYPE>
+struct FmtSmall : Fmt<TYPE> {
+    static constexpr int kUnitsPerTile = 32;
+    static constexpr int kTileBytes = Fmt<TYPE>::kUnitBytes * 32;
+    static constexpr int kStageBytes = kTileBytes + 16;
+    static constexpr int kStages = TYPE == GQ_TYPE_Q4_K ? 3 : 2;
+};
 
 // Minimum resident CTAs per SM the Q4_K kernel is compiled for (caps its registers; the
 // other formats leave the register count to the compiler).
@@ -764,11 +782,11 @@ __device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int 
 // The persistent per-warp pipeline shared by all block formats
 // ---------------------------------------------------------------------------------------
 
-template <int TYPE, int MODE>
+template <int TYPE, int MODE, bool SMALL = false>
 __global__ void __launch_bounds__(Fmt<TYPE>::kThreads,
                                   TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS : (TYPE == GQ_TYPE_Q5_K ? 2 : 1))
     gq_convert_kernel(const __grid_constant__ GqBatch batch) {
-    using F = Fmt<TYPE>;
+    using F = typename std::conditional<SMALL, FmtSmall<TYPE>, Fmt<TYPE>>::type;
     constexpr bool kBulk = F::kBulk;
     extern __shared__ __align__(16) uint8_t smem[];
     // exact reciprocals 1/k, k = 1..16, for the block-scale division of requant_block
@@ -1205,32 +1223,66 @@ DeviceInfo& device_info() {
     return di;
 }
 
-template <int TYPE, int MODE>
-int launch_fmt(const GqBatch& b, cudaStream_t s) {
-    using F = Fmt<TYPE>;
-    constexpr int smem = F::kWarps * F::kStages * F::kStageBytes;
-    static_assert(smem <= 200 * 1024, "dynamic shared memory per CTA");
+// Resident CTAs per SM of one kernel instance on the current device (queried once).
+template <int TYPE, int MODE, bool SMALL>
+int occupancy(int smem) {
     static int per_sm[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     int& occ = per_sm[dev & 63];
     if (occ == 0) {
         if (smem > 48 * 1024)
-            cudaFuncSetAttribute(gq_convert_kernel<TYPE, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gq_convert_kernel<TYPE, MODE>, F::kThreads, smem) !=
-                cudaSuccess || occ < 1)
+            cudaFuncSetAttribute(gq_convert_kernel<TYPE, MODE, SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gq_convert_kernel<TYPE, MODE, SMALL>,
+                                                          Fmt<TYPE>::kThreads, smem) != cudaSuccess ||
+            occ < 1)
             occ = 1;
     }
+    return occ;
+}
+
+template <int TYPE, int MODE, bool SMALL = false>
+int launch_fmt(const GqBatch& b, cudaStream_t s) {
+    using F = typename std::conditional<SMALL, FmtSmall<TYPE>, Fmt<TYPE>>::type;
+    constexpr int smem = F::kWarps * F::kStages * F::kStageBytes;
+    static_assert(smem <= 200 * 1024, "dynamic shared memory per CTA");
+    const int occ = occupancy<TYPE, MODE, SMALL>(smem);
     const int64_t want = (b.total_tiles + F::kWarps - 1) / F::kWarps;
     const int64_t cap = static_cast<int64_t>(device_info().sms) * occ;
     const int blocks = static_cast<int>(want < cap ? want : cap);
     if (blocks <= 0) return 0;
-    gq_convert_kernel<TYPE, MODE><<<blocks, F::kThreads, smem, s>>>(b);
+    gq_convert_kernel<TYPE, MODE, SMALL><<<blocks, F::kThreads, smem, s>>>(b);
     return static_cast<int>(cudaGetLastError());
+}
+
+// Q4_K / Q5_K: a launch with fewer than 8 tiles per resident warp goes out in the small
+// tiles, its batch renumbered for them (the host copy of the parameter block is the cost).
+template <int TYPE, int MODE>
+int launch_k45(const GqBatch& b, cudaStream_t s) {
+    using F = Fmt<TYPE>;
+    constexpr int smem = F::kWarps * F::kStages * F::kStageBytes;
+    const int64_t warps = static_cast<int64_t>(device_info().sms) * occupancy<TYPE, MODE, false>(smem) * F::kWarps;
+    if (b.total_tiles >= 8 * warps) return launch_fmt<TYPE, MODE, false>(b, s);
+    std::unique_ptr<GqBatch> sb(new (std::nothrow) GqBatch(b));
+    if (!sb) return static_cast<int>(cudaErrorMemoryAllocation);
+    sb->total_tiles = 0;
+    for (int i = 0; i < sb->n; ++i) {
+        sb->d[i].tile_begin = sb->total_tiles;
+        sb->total_tiles += (sb->d[i].n_units + FmtSmall<TYPE>::kUnitsPerTile - 1) / FmtSmall<TYPE>::kUnitsPerTile;
+    }
+    return launch_fmt<TYPE, MODE, true>(*sb, s);
 }
 
 template <int TYPE>
 int launch_modes(int out_mask, const GqBatch& b, cudaStream_t s) {
+    if constexpr (TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K) {
+        switch (out_mask) {
+            case kOutCodes: return launch_k45<TYPE, kOutCodes>(b, s);
+            case kOutF32: return launch_k45<TYPE, kOutF32>(b, s);
+            default: return launch_k45<TYPE, kOutCodes | kOutF32>(b, s);
+        }
+    }
     switch (out_mask) {
         case kOutCodes: return launch_fmt<TYPE, kOutCodes>(b, s);
         case kOutF32: return launch_fmt<TYPE, kOutF32>(b, s);
