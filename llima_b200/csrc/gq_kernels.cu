@@ -47,7 +47,7 @@ namespace gq {
 #define GQ_K45_WARPS 8
 #endif
 #ifndef GQ_Q6K_SUB
-#define GQ_Q6K_SUB 1
+#define GQ_Q6K_SUB 2
 #endif
 #ifndef GQ_Q6K_STAGES
 #define GQ_Q6K_STAGES 3
@@ -73,6 +73,12 @@ struct Fmt;
 #ifndef GQ_Q0_BULK
 #define GQ_Q0_BULK 1
 #endif
+#ifndef GQ_Q0_SUB
+#define GQ_Q0_SUB 8
+#endif
+#ifndef GQ_Q0_STAGES
+#define GQ_Q0_STAGES 2
+#endif
 
 #define GQ_FMT(TYPE, UNIT_BYTES, UNITS_PER_TILE, STAGES, WARPS, BULK)                     \
     template <>                                                                           \
@@ -92,8 +98,8 @@ struct Fmt;
 GQ_FMT(GQ_TYPE_Q4_K, 144, 8 * GQ_K45_SUB, GQ_K45_STAGES, GQ_K45_WARPS, true)   // sub-tiles of 8 super-blocks
 GQ_FMT(GQ_TYPE_Q5_K, 176, 8 * GQ_Q5K_SUB, GQ_Q5K_STAGES, GQ_Q5K_WARPS, true)
 GQ_FMT(GQ_TYPE_Q6_K, 210, 8 * GQ_Q6K_SUB, GQ_Q6K_STAGES, 8, GQ_Q6K_BULK)   // sub-tiles of 128 blocks of 16
-GQ_FMT(GQ_TYPE_Q8_0, 34, 32, 4, 8, GQ_Q0_BULK)   // 32 blocks of 32 per tile
-GQ_FMT(GQ_TYPE_Q4_0, 18, 32, 4, 8, GQ_Q0_BULK)
+GQ_FMT(GQ_TYPE_Q8_0, 34, 32 * GQ_Q0_SUB, GQ_Q0_STAGES, 8, GQ_Q0_BULK)   // sub-tiles of 32 blocks of 32
+GQ_FMT(GQ_TYPE_Q4_0, 18, 32 * GQ_Q0_SUB, GQ_Q0_STAGES, 8, GQ_Q0_BULK)
 GQ_FMT(GQ_TYPE_Q4_1, 20, 32, 4, 8, GQ_Q0_BULK)   // 32 blocks of 32 per tile, one per lane
 GQ_FMT(GQ_TYPE_Q5_0, 22, 32, 4, 8, GQ_Q0_BULK)
 GQ_FMT(GQ_TYPE_Q5_1, 24, 32, 4, 8, GQ_Q0_BULK)
@@ -105,12 +111,16 @@ GQ_FMT(GQ_TYPE_Q3_K, 110, 8, 4, 8, GQ_Q0_BULK)
 // config, a host call's piece) use 4 sub-tiles per tile instead (Q4_K with 3 stages): the
 // C2 Q4_K 11008x4096 tensor alone measured 0.585 of the copy peak so against 0.485 in the
 // big tiles, and 0.559 with 1 sub-tile x 6 stages.
+// Q8_0 / Q4_0 likewise: big launches in tiles of 8 x 32 blocks with 2 stages (Qwen2.5-7B
+// Q8_0 embedding and output 0.98 of the copy peak against 0.82 in 32-block tiles), small
+// ones in 32-block tiles with 4 stages (C1 0.72 against 0.52 in the big tiles).
 template <int TYPE>
 struct FmtSmall : Fmt<TYPE> {
+    static constexpr bool kQ0 = TYPE == GQ_TYPE_Q8_0 || TYPE == GQ_TYPE_Q4_0;
     static constexpr int kUnitsPerTile = 32;
     static constexpr int kTileBytes = Fmt<TYPE>::kUnitBytes * 32;
     static constexpr int kStageBytes = kTileBytes + 16;
-    static constexpr int kStages = TYPE == GQ_TYPE_Q4_K ? 3 : 2;
+    static constexpr int kStages = kQ0 ? 4 : (TYPE == GQ_TYPE_Q4_K ? 3 : 2);
 };
 
 // Minimum resident CTAs per SM the Q4_K kernel is compiled for (caps its registers; the
@@ -879,7 +889,14 @@ __global__ void __launch_bounds__(Fmt<TYPE>::kThreads,
             if (MODE & kOutCodes) acc.retarget(D.diag, lane);
             process_k16<TYPE, MODE>(D, unit0, nunits, tile, lane, acc, recip);
         } else {
-            process_q0<TYPE == GQ_TYPE_Q4_0, MODE>(D, unit0, nunits, tile, lane);
+            // Q8_0 / Q4_0: sub-tiles of 32 blocks
+#pragma unroll 1
+            for (int j = 0; j < F::kUnitsPerTile / 32; ++j) {
+                const int rest = nunits - 32 * j;
+                if (rest <= 0) break;
+                process_q0<TYPE == GQ_TYPE_Q4_0, MODE>(D, unit0 + 32 * j, rest < 32 ? rest : 32,
+                                                       tile + 32 * j * F::kUnitBytes, lane);
+            }
         }
         __syncwarp();
         stage = (stage + 1 == F::kStages) ? 0 : stage + 1;
@@ -1256,8 +1273,9 @@ int launch_fmt(const GqBatch& b, cudaStream_t s) {
     return static_cast<int>(cudaGetLastError());
 }
 
-// Q4_K / Q5_K: a launch with fewer than 8 tiles per resident warp goes out in the small
-// tiles, its batch renumbered for them (the host copy of the parameter block is the cost).
+// Q4_K / Q5_K / Q8_0 / Q4_0: a launch with fewer than 8 tiles per resident warp goes out
+// in the small tiles, its batch renumbered for them (the host copy of the parameter block
+// is the cost).
 template <int TYPE, int MODE>
 int launch_k45(const GqBatch& b, cudaStream_t s) {
     using F = Fmt<TYPE>;
@@ -1276,7 +1294,7 @@ int launch_k45(const GqBatch& b, cudaStream_t s) {
 
 template <int TYPE>
 int launch_modes(int out_mask, const GqBatch& b, cudaStream_t s) {
-    if constexpr (TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K) {
+    if constexpr (TYPE == GQ_TYPE_Q4_K || TYPE == GQ_TYPE_Q5_K || TYPE == GQ_TYPE_Q8_0 || TYPE == GQ_TYPE_Q4_0) {
         switch (out_mask) {
             case kOutCodes: return launch_k45<TYPE, kOutCodes>(b, s);
             case kOutF32: return launch_k45<TYPE, kOutF32>(b, s);
