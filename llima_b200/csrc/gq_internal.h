@@ -79,7 +79,7 @@ int kernel_errors(bool clear, uint32_t* flags);
 int launch_batch(int type, int out_mask, const GqBatch& batch, void* stream);
 int64_t tiles_for(int type, int64_t n_units);
 int launch_modalix(int type, const GqModalixBatch& b, void* stream);
-constexpr int kModalixRows = 128;   // output channels per tile of the fused layout writer
+constexpr int kModalixRows = 64;    // output channels per tile of the fused layout writer
 constexpr int kModalixCols = 256;   // input channels per tile
 int launch_layout(const uint8_t* codes, const float* scales, int64_t rows, int64_t cols, int64_t nb,
                   int64_t rows_padded, uint8_t* out_codes, float* out_scales, void* stream);

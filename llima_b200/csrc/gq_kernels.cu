@@ -1025,9 +1025,10 @@ struct MxFmt {
     static constexpr int CH = STR / 16;                     // 16-byte chunks per slot
     static constexpr int NBS = 256 / (TYPE == GQ_TYPE_Q6_K || TYPE == GQ_TYPE_Q2_K || TYPE == GQ_TYPE_Q3_K ? 16 : 32);
     static constexpr int kWarpStaging = 16 * STR + 16;      // + slack for lds128_align2
-    static constexpr int kTBytes = kModalixCols * kModalixRows;   // column tile (bytes)
-    static constexpr int kRBytes = kModalixRows * kModalixCols;   // row tile
-    static constexpr int kSBytes = kModalixRows * 16 * 4;         // scale tile (up to 16 per row)
+    // the CTA's two workers share one column tile and split the row and scale tiles
+    static constexpr int kTBytes = kModalixCols * 2 * kModalixRows;   // column tile (bytes)
+    static constexpr int kRBytes = 2 * kModalixRows * kModalixCols;   // row tile
+    static constexpr int kSBytes = 2 * kModalixRows * 16 * 4;         // scale tile (up to 16 per row)
     static constexpr int kSmem = kTBytes + kRBytes + kSBytes + 8 * kWarpStaging + 4096;   // + alignment
 };
 
@@ -1058,17 +1059,31 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
     const uint32_t s_s = smem_u32addr(stile);
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
+    // Two independent workers per CTA: warps 0-3 and 4-7, each with its own tiles (64 output
+    // channels x 256 input channels), its half of the row and scale tiles, its chunks of the
+    // column tile and its own block barrier, so that one worker's decode overlaps the
+    // other's transpose and stores.
+    const int half = warp >> 2;           // worker
+    const int wq = warp & 3;              // warp within the worker
+    const int hid = threadIdx.x & 127;    // thread within the worker
+    auto worker_sync = [&]() {
+        if (half == 0) {
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+        } else {
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+        }
+    };
     uint8_t* staging = smem + X::kTBytes + X::kRBytes + X::kSBytes + warp * X::kWarpStaging;
     __syncthreads();
 
-    // a CTA visits its tiles in increasing order, so each tensor cursor only moves forward
+    // a worker visits its tiles in increasing order, so each tensor cursor only moves forward
     int c_issue = 0, c_tile = 0;
     auto seek = [&](int& c, uint32_t t) -> const GqModalix& {
         while (c + 1 < b.n && b.d[c + 1].tile_begin <= t) ++c;
         return b.d[c];
     };
 
-    // tile t of the batch: tensor m, row block rb (output channels d0..d0+127), column
+    // tile t of the batch: tensor m, row block rb (output channels d0..d0+63), column
     // block cb (256 input channels)
     auto issue = [&](uint32_t t) {
         if (t >= b.total_tiles) return;
@@ -1076,7 +1091,7 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
         const uint32_t lt = t - m.tile_begin;
         const uint32_t rb = fast_div(lt, m.ncol_mul, m.ncol_shift), cb = lt - rb * m.n_col_tiles;
         const uint32_t rows = static_cast<uint32_t>(m.rows);
-        const uint32_t o_lane = rb * kModalixRows + 16 * warp + (lane & 15);
+        const uint32_t o_lane = rb * kModalixRows + 16 * wq + (lane & 15);
         // lanes 0..15: byte offset of row (lane)'s segment, or -1 past the last row
         int64_t seg = -1;
         if (o_lane < rows)
@@ -1099,16 +1114,17 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
     dt.codes = rtile;
     dt.scales = stile;
 
-    uint32_t t = blockIdx.x;
+    const uint32_t workers = 2 * gridDim.x;
+    uint32_t t = 2 * blockIdx.x + half;
     issue(t);
-    for (; t < b.total_tiles; t += gridDim.x) {
+    for (; t < b.total_tiles; t += workers) {
         const GqModalix& m = seek(c_tile, t);
         acc.retarget(m.diag, lane);
         const uint32_t lt = t - m.tile_begin;
         const uint32_t rb = fast_div(lt, m.ncol_mul, m.ncol_shift), cb = lt - rb * m.n_col_tiles;
         const uint32_t rows = static_cast<uint32_t>(m.rows);
         const uint32_t d0 = rb * kModalixRows;
-        // rows of this tile below `rows` (0..128)
+        // rows of this tile below `rows` (0..64)
         const int valid_rows = d0 >= rows ? 0 : (rows - d0 < kModalixRows ? static_cast<int>(rows - d0) : kModalixRows);
         const int shift = static_cast<int>((cb * X::SEG) & 15);   // row starts are 16-byte aligned
         cp_async_wait<0>();
@@ -1117,7 +1133,7 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
         if constexpr (X::K) {
 #pragma unroll 1
             for (int sub = 0; sub < 2; ++sub) {
-                const int left = valid_rows - (16 * warp + 8 * sub);
+                const int left = valid_rows - (16 * wq + 8 * sub);
                 const int n = left <= 0 ? 0 : (left < 8 ? left : 8);
                 if (n == 0) continue;
                 const uint8_t* tile = staging + 8 * sub * X::STR + shift;
@@ -1133,7 +1149,7 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
         } else {
 #pragma unroll 1
             for (int j = 0; j < 4; ++j) {
-                const int left = valid_rows - (16 * warp + 4 * j);
+                const int left = valid_rows - (16 * wq + 4 * j);
                 const int n = left <= 0 ? 0 : (left < 4 ? left * 8 : 32);
                 if (n == 0) continue;
                 const uint8_t* tile = staging + 4 * j * X::STR;
@@ -1145,12 +1161,13 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
                 }
             }
         }
-        __syncthreads();
+        worker_sync();
         // phase B: the next tile's copies go out; transpose codes into the column tile.  A
-        // thread takes 16 output channels (rows 16a..16a+15 of the row tile) x 4 input
-        // channels (4b..4b+3): 4x4-byte blocks swapped by PRMT, and each input channel's 16
-        // bytes stored at chunk a ^ (b & 7) of its 128-byte column-tile row
-        issue(t + gridDim.x);
+        // thread takes 16 output channels (rows 16a..16a+15 of the row tile, a = warp: the
+        // worker's rows are 64 half.. ) x 4 input channels (4b..4b+3): 4x4-byte blocks
+        // swapped by PRMT, and each input channel's 16 bytes stored at chunk a ^ (b & 7) of
+        // its 128-byte column-tile row (the two workers' chunks never coincide)
+        issue(t + workers);
         const bool full = valid_rows == kModalixRows;
 #pragma unroll 1
         for (int it = 0; it < 2; ++it) {
@@ -1164,7 +1181,7 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
                 for (int mm = 0; mm < 4; ++mm) {
                     const int r = 16 * a + 4 * j + mm;   // r % 16 = 4j + mm: the swizzle key
                     const uint32_t addr = r_s + r * 256 + ((((b >> 2) ^ (4 * j + mm)) << 4) | ((b & 3) << 2));
-                    x[mm] = (full || r < valid_rows) ? lds_u32(addr) : 0u;
+                    x[mm] = (full || r - 64 * half < valid_rows) ? lds_u32(addr) : 0u;
                 }
                 const uint32_t t0 = __byte_perm(x[0], x[1], 0x5140), t1 = __byte_perm(x[0], x[1], 0x7362);
                 const uint32_t t2 = __byte_perm(x[2], x[3], 0x5140), t3 = __byte_perm(x[2], x[3], 0x7362);
@@ -1179,14 +1196,16 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
                 sts(t_s + (4 * b + k) * 128 + chunk, make_uint4(y[0][k], y[1][k], y[2][k], y[3][k]));
         }
         const int64_t rp = m.rows_padded;
-        for (int task = threadIdx.x; task < X::NBS * 32; task += 256) {
+        for (int task = hid; task < X::NBS * 16; task += 128) {
             const int bb = task % X::NBS, quad = task / X::NBS;   // scale column, 4 output channels
             const int64_t o0 = d0 + 4 * quad;
             if (o0 >= rp) continue;
             float v[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-                v[e] = (4 * quad + e < valid_rows) ? __uint_as_float(lds_u32(s_s + 4 * ((4 * quad + e) * X::NBS + bb))) : 1.0f;
+                v[e] = (4 * quad + e < valid_rows)
+                           ? __uint_as_float(lds_u32(s_s + 4 * ((64 * half + 4 * quad + e) * X::NBS + bb)))
+                           : 1.0f;
             float* dst = m.out_scales + static_cast<int64_t>(cb * X::NBS + bb) * rp + o0;
             if (o0 + 4 <= rp && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
                 st_global(reinterpret_cast<float4*>(dst), make_float4(v[0], v[1], v[2], v[3]));
@@ -1194,16 +1213,18 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
                 for (int e = 0; e < 4 && o0 + e < rp; ++e) st_global(dst + e, v[e]);
             }
         }
-        __syncthreads();
-        // phase C: column tile -> codes, 16 output channels per lane
-        const int q = lane & 7;                                               // output channels 16q..16q+15
-        const int64_t o0 = d0 + 16 * q;
+        worker_sync();
+        // phase C: column tile -> codes, 16 output channels per lane: lanes 4s + l of a
+        // quarter warp take output channels 16l.. of input channels i and i + 16, whose
+        // chunks (q ^ u and q ^ u ^ 4) fill all eight 16-byte bank groups
+        const int q = 4 * half + (lane & 3);                                  // row-tile group of 16
+        const int64_t o0 = d0 + 16 * (lane & 3);
         const bool seg_full = o0 + 16 <= rp;
         if (o0 < rp) {
 #pragma unroll 4
             for (int it = 0; it < 8; ++it) {
-                const int idx = warp * 8 + it;
-                const int i = 16 * (idx >> 2) + (idx & 3) + 4 * (lane >> 3);   // input channel in the tile
+                const int idx = wq * 8 + it;
+                const int i = 32 * (idx >> 2) + 4 * (idx & 3) + 16 * ((lane >> 2) & 1) + (lane >> 3);
                 const uint4 w = lds_v4(t_s + i * 128 + ((q ^ ((i >> 2) & 7)) << 4));
                 uint8_t* dst = m.out_codes + static_cast<int64_t>(cb * kModalixCols + i) * rp + o0;
                 if (seg_full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
@@ -1356,7 +1377,8 @@ int launch_modalix_t(const GqModalixBatch& m, cudaStream_t s) {
             occ = 1;
     }
     const int64_t cap = static_cast<int64_t>(device_info().sms) * occ;
-    const int blocks = static_cast<int>(m.total_tiles < cap ? m.total_tiles : cap);
+    const int64_t want = (static_cast<int64_t>(m.total_tiles) + 1) / 2;   // two workers per CTA
+    const int blocks = static_cast<int>(want < cap ? want : cap);
     if (blocks <= 0) return 0;
     gq_modalix_kernel<TYPE><<<blocks, 256, X::kSmem, s>>>(m);
     return static_cast<int>(cudaGetLastError());
