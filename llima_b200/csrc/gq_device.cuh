@@ -420,11 +420,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 
 // ---- code / scale stores of a conversion ---------------------------------------------
 
-// Shared row tiles of 256-byte rows (the fused Modalix writer) keep their 16-byte chunks
-// XOR-swizzled by row: chunk c of the row at shared-address bits 8..11 = r sits at chunk
-// c ^ r, so that the decode's stores (lanes 64 or 16 bytes apart over 8 rows) and the
-// transpose's column reads spread over all banks.  A bijection on every 256-byte block.
-__device__ __forceinline__ uint32_t row_swizzle(uint32_t a) { return a ^ (((a >> 8) & 15u) << 4); }
+// Shared row tiles of 256-byte rows (the fused Modalix writer, 512-byte aligned) keep their
+// 16-byte chunks swizzled: chunk c of row r sits at chunk c ^ (2 (r & 1) + (c >> 3)).  A
+// quarter warp's 16-byte stores then fill all eight bank groups in every decode pattern:
+// Q4_K / Q5_K lanes 64 bytes apart over 2 rows, Q6_K and the 16-value K formats lanes 16
+// bytes apart, Q8_0 / Q4_0 32-byte units; and a warp reading 8 chunks of one row (the
+// transpose) touches 32 distinct banks.  A bijection on every 256-byte row.
+__device__ __forceinline__ uint32_t row_swizzle(uint32_t a) {
+    return a ^ (((((a >> 8) & 1u) << 1) | ((a >> 7) & 1u)) << 4);
+}
 
 __device__ __forceinline__ void sts(uint32_t a, uint8_t v) {
     asm volatile("st.shared.u8 [%0], %1;" ::"r"(a), "r"(static_cast<uint32_t>(v)) : "memory");

@@ -1049,8 +1049,8 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
     extern __shared__ __align__(16) uint8_t smem_raw[];
     __shared__ float recip[17];
     if (threadIdx.x < 17) recip[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, static_cast<float>(threadIdx.x)) : 0.0f;
-    // the tiles start on a 4 KiB boundary: the row tile's swizzle key (shared-address bits
-    // 8..11) is then the row index mod 16
+    // the tiles start on a 4 KiB boundary: the row tile's swizzle key (shared-address bit 8)
+    // is then the row index mod 2
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 4095) & ~uintptr_t(4095));
     uint8_t* rtile = smem + X::kTBytes;                                        // 128 rows x 256 bytes
     float* stile = reinterpret_cast<float*>(smem + X::kTBytes + X::kRBytes);   // 128 rows x NBS
@@ -1179,8 +1179,8 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
                 uint32_t x[4];
 #pragma unroll
                 for (int mm = 0; mm < 4; ++mm) {
-                    const int r = 16 * a + 4 * j + mm;   // r % 16 = 4j + mm: the swizzle key
-                    const uint32_t addr = r_s + r * 256 + ((((b >> 2) ^ (4 * j + mm)) << 4) | ((b & 3) << 2));
+                    const int r = 16 * a + 4 * j + mm;   // r % 2 = mm % 2; chunk b >> 2 has bit 3 = it
+                    const uint32_t addr = r_s + r * 256 + ((((b >> 2) ^ (2 * (mm & 1) + it)) << 4) | ((b & 3) << 2));
                     x[mm] = (full || r - 64 * half < valid_rows) ? lds_u32(addr) : 0u;
                 }
                 const uint32_t t0 = __byte_perm(x[0], x[1], 0x5140), t1 = __byte_perm(x[0], x[1], 0x7362);
