@@ -420,14 +420,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 
 // ---- code / scale stores of a conversion ---------------------------------------------
 
-// Shared row tiles of 256-byte rows (the fused Modalix writer, 512-byte aligned) keep their
-// 16-byte chunks swizzled: chunk c of row r sits at chunk c ^ (2 (r & 1) + (c >> 3)).  A
-// quarter warp's 16-byte stores then fill all eight bank groups in every decode pattern:
-// Q4_K / Q5_K lanes 64 bytes apart over 2 rows, Q6_K and the 16-value K formats lanes 16
-// bytes apart, Q8_0 / Q4_0 32-byte units; and a warp reading 8 chunks of one row (the
-// transpose) touches 32 distinct banks.  A bijection on every 256-byte row.
+// Shared row tiles of 256-byte rows (the fused Modalix writer, 8 KiB aligned) keep their
+// 16-byte chunks swizzled: chunk c of row r sits at chunk c ^ g(r) ^ 3 (c >> 3), with
+// g(r) = (r & 3) | 4 ((r >> 4) & 1).  A quarter warp's 16-byte stores then fill all eight
+// bank groups in every decode pattern (Q4_K / Q5_K: lanes 64 bytes apart over a row pair;
+// Q6_K and the 16-value K formats: 8 consecutive chunks of a row; Q8_0 / Q4_0: 32-byte
+// units), and so do the 8 rows {4m + e, 16 + 4m + e} (e < 4) that one ldmatrix phase of the
+// transpose reads at one chunk.  A bijection on every 256-byte row.
 __device__ __forceinline__ uint32_t row_swizzle(uint32_t a) {
-    return a ^ (((((a >> 8) & 1u) << 1) | ((a >> 7) & 1u)) << 4);
+    const uint32_t g = ((a >> 8) & 3u) | (((a >> 12) & 1u) << 2);
+    return a ^ ((g ^ (3u * ((a >> 7) & 1u))) << 4);
+}
+
+// Two 16x16 byte matrices transposed out of shared memory: lanes 0-15 give the row addresses
+// of matrix 0, lanes 16-31 those of matrix 1.  Lane t receives, of matrix m, column t / 4
+// (register 2m) and column t / 4 + 8 (register 2m + 1), rows 4 (t % 4)..4 (t % 4) + 3 in
+// its bytes 0..3.
+__device__ __forceinline__ void ldsm_x2_trans_b8(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m16n16.x2.trans.shared.b8 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(a)
+                 : "memory");
 }
 
 __device__ __forceinline__ void sts(uint32_t a, uint8_t v) {

@@ -1001,16 +1001,17 @@ __global__ void __launch_bounds__(kThreads) gq_requant_kernel(const float* __res
 // sima_lmm/model/model_graph.py:1012-1079): codes (rows, cols) -> (cols, rows_padded) and
 // block scales (rows, cols / B) -> (cols / B, rows_padded), written in one pass.
 //
-// A CTA owns a tile of 128 output channels (rows of the converted tensor in output order;
-// the llama q/k head permutation becomes a gather of source rows) x 256 input channels.
-// Each warp copies the stored bytes of its 16 rows with cp.async: the 16-byte-aligned span
-// around each row's segment, so a unit sits `shift` bytes into its slot (0 unless the
-// unit size is not a multiple of 16).  The format's decode runs unchanged with its code /
-// scale stores directed to a shared row tile (kOutSmem).  The row tile is transposed in
-// 4x4-byte blocks (PRMT) into a column tile whose 4-byte words are XOR-swizzled by row,
-// so that both the transpose and the final read are free of bank conflicts, and written
-// out as 16-byte stores along output channels.  Output channels rows..rows_padded-1 are
-// the layout's padding: zero codes and unit scales.
+// A CTA runs two workers of 4 warps; a worker owns a tile of 64 output channels (rows of
+// the converted tensor in output order; the llama q/k head permutation becomes a gather of
+// source rows) x 256 input channels.  Each warp copies the stored bytes of its 16 rows
+// with cp.async: the 16-byte-aligned span around each row's segment, so a unit sits
+// `shift` bytes into its slot (0 unless the unit size is not a multiple of 16).  The
+// format's decode runs unchanged with its code / scale stores directed to a shared row
+// tile (kOutSmem).  The row tile is transposed by ldmatrix (.m16n16 .trans .b8: a thread
+// receives 4 consecutive rows of one column) with the rows of each 16x16 matrix chosen so
+// that a lane ends up holding 16 consecutive output channels of 2 input channels, written
+// out as 16-byte stores: a quarter warp covers 64 contiguous bytes of 2 input channels.
+// Output channels rows..rows_padded-1 are the layout's padding: zero codes and unit scales.
 // ---------------------------------------------------------------------------------------
 
 template <int TYPE>
@@ -1025,11 +1026,9 @@ struct MxFmt {
     static constexpr int CH = STR / 16;                     // 16-byte chunks per slot
     static constexpr int NBS = 256 / (TYPE == GQ_TYPE_Q6_K || TYPE == GQ_TYPE_Q2_K || TYPE == GQ_TYPE_Q3_K ? 16 : 32);
     static constexpr int kWarpStaging = 16 * STR + 16;      // + slack for lds128_align2
-    // the CTA's two workers share one column tile and split the row and scale tiles
-    static constexpr int kTBytes = kModalixCols * 2 * kModalixRows;   // column tile (bytes)
-    static constexpr int kRBytes = 2 * kModalixRows * kModalixCols;   // row tile
-    static constexpr int kSBytes = 2 * kModalixRows * 16 * 4;         // scale tile (up to 16 per row)
-    static constexpr int kSmem = kTBytes + kRBytes + kSBytes + 8 * kWarpStaging + 4096;   // + alignment
+    static constexpr int kRBytes = 2 * kModalixRows * kModalixCols;   // row tile, both workers
+    static constexpr int kSBytes = 2 * kModalixRows * NBS * 4;        // scale tile, both workers
+    static constexpr int kSmem = kRBytes + kSBytes + 8 * kWarpStaging + 8192;   // + alignment
 };
 
 // Source row of output channel o (inverse of the q/k permutation of
@@ -1049,20 +1048,18 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
     extern __shared__ __align__(16) uint8_t smem_raw[];
     __shared__ float recip[17];
     if (threadIdx.x < 17) recip[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, static_cast<float>(threadIdx.x)) : 0.0f;
-    // the tiles start on a 4 KiB boundary: the row tile's swizzle key (shared-address bit 8)
-    // is then the row index mod 2
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 4095) & ~uintptr_t(4095));
-    uint8_t* rtile = smem + X::kTBytes;                                        // 128 rows x 256 bytes
-    float* stile = reinterpret_cast<float*>(smem + X::kTBytes + X::kRBytes);   // 128 rows x NBS
-    const uint32_t t_s = smem_u32addr(smem);                                   // 256 rows x 32 words
+    // the row tile starts on an 8 KiB boundary: its swizzle key (shared-address bits 8, 9
+    // and 12) is then made of bits 0, 1 and 4 of the row index
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 8191) & ~uintptr_t(8191));
+    uint8_t* rtile = smem;                                         // 128 rows x 256 bytes
+    float* stile = reinterpret_cast<float*>(smem + X::kRBytes);    // 128 rows x NBS
     const uint32_t r_s = smem_u32addr(rtile);
     const uint32_t s_s = smem_u32addr(stile);
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     // Two independent workers per CTA: warps 0-3 and 4-7, each with its own tiles (64 output
-    // channels x 256 input channels), its half of the row and scale tiles, its chunks of the
-    // column tile and its own block barrier, so that one worker's decode overlaps the
-    // other's transpose and stores.
+    // channels x 256 input channels), its half of the row and scale tiles and its own block
+    // barrier, so that one worker's decode overlaps the other's transpose and stores.
     const int half = warp >> 2;           // worker
     const int wq = warp & 3;              // warp within the worker
     const int hid = threadIdx.x & 127;    // thread within the worker
@@ -1073,7 +1070,7 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
             asm volatile("bar.sync 2, 128;" ::: "memory");
         }
     };
-    uint8_t* staging = smem + X::kTBytes + X::kRBytes + X::kSBytes + warp * X::kWarpStaging;
+    uint8_t* staging = smem + X::kRBytes + X::kSBytes + warp * X::kWarpStaging;
     __syncthreads();
 
     // a worker visits its tiles in increasing order, so each tensor cursor only moves forward
@@ -1092,19 +1089,17 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
         const uint32_t rb = fast_div(lt, m.ncol_mul, m.ncol_shift), cb = lt - rb * m.n_col_tiles;
         const uint32_t rows = static_cast<uint32_t>(m.rows);
         const uint32_t o_lane = rb * kModalixRows + 16 * wq + (lane & 15);
-        // lanes 0..15: byte offset of row (lane)'s segment, or -1 past the last row
-        int64_t seg = -1;
-        if (o_lane < rows)
-            seg = (static_cast<int64_t>(modalix_src_row(m, o_lane)) * m.units_per_row + cb * X::UNITS) * X::UB;
-        // every lane runs the same trips (the shuffle needs the whole warp)
-        for (int base = 0; base < 16 * X::CH; base += 32) {
-            const int q = base + lane;
-            const int lr = q < 16 * X::CH ? q / X::CH : 15, c = q - lr * X::CH;
-            const int64_t off = __shfl_sync(0xffffffffu, seg, lr);
-            if (q >= 16 * X::CH || off < 0) continue;
-            const int64_t start = (off & ~int64_t(15)) + 16 * c, end = off + X::SEG;
-            if (start >= end) continue;
-            cp_async16(staging + lr * X::STR + 16 * c, m.src + start, end - start < 16 ? static_cast<int>(end - start) : 16);
+        // lanes l and l + 16 copy row l & 15's segment (the 16-byte-aligned span around it),
+        // alternate 16-byte chunks each
+        if (o_lane < rows) {
+            const int64_t off = (static_cast<int64_t>(modalix_src_row(m, o_lane)) * m.units_per_row + cb * X::UNITS) * X::UB;
+            const int64_t end = off + X::SEG;
+            uint8_t* dst = staging + (lane & 15) * X::STR;
+#pragma unroll
+            for (int c = lane >> 4; c < X::CH; c += 2) {
+                const int64_t start = (off & ~int64_t(15)) + 16 * c;
+                if (start < end) cp_async16(dst + 16 * c, m.src + start, end - start < 16 ? static_cast<int>(end - start) : 16);
+            }
         }
         cp_async_commit();
     };
@@ -1161,51 +1156,67 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
                 }
             }
         }
-        worker_sync();
-        // phase B: the next tile's copies go out; transpose codes into the column tile.  A
-        // thread takes 16 output channels (rows 16a..16a+15 of the row tile, a = warp: the
-        // worker's rows are 64 half.. ) x 4 input channels (4b..4b+3): 4x4-byte blocks
-        // swapped by PRMT, and each input channel's 16 bytes stored at chunk a ^ (b & 7) of
-        // its 128-byte column-tile row (the two workers' chunks never coincide)
-        issue(t + workers);
-        const bool full = valid_rows == kModalixRows;
-#pragma unroll 1
-        for (int it = 0; it < 2; ++it) {
-            const int a = warp;
-            const int b = lane + 32 * it;
-            uint32_t y[4][4];   // [row group j][input channel k]
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                uint32_t x[4];
-#pragma unroll
-                for (int mm = 0; mm < 4; ++mm) {
-                    const int r = 16 * a + 4 * j + mm;   // r % 2 = mm % 2; chunk b >> 2 has bit 3 = it
-                    const uint32_t addr = r_s + r * 256 + ((((b >> 2) ^ (2 * (mm & 1) + it)) << 4) | ((b & 3) << 2));
-                    x[mm] = (full || r - 64 * half < valid_rows) ? lds_u32(addr) : 0u;
-                }
-                const uint32_t t0 = __byte_perm(x[0], x[1], 0x5140), t1 = __byte_perm(x[0], x[1], 0x7362);
-                const uint32_t t2 = __byte_perm(x[2], x[3], 0x5140), t3 = __byte_perm(x[2], x[3], 0x7362);
-                y[j][0] = __byte_perm(t0, t2, 0x5410);
-                y[j][1] = __byte_perm(t0, t2, 0x7632);
-                y[j][2] = __byte_perm(t1, t3, 0x5410);
-                y[j][3] = __byte_perm(t1, t3, 0x7632);
+        // rows of the worker's half at or past valid_rows are layout padding: zero codes and
+        // unit scales in the row and scale tiles, so that the transpose reads every row
+        {
+            const int first = valid_rows > 16 * wq ? valid_rows - 16 * wq : 0;
+            if (first < 16) {
+                __syncwarp();
+                const uint32_t r0 = r_s + (16 * warp + first) * 256;
+                for (int q = lane; q < (16 - first) * 16; q += 32) sts(r0 + 16 * q, make_uint4(0u, 0u, 0u, 0u));
+                const uint32_t s0 = s_s + 4 * (16 * warp + first) * X::NBS;
+                for (int q = lane; q < (16 - first) * X::NBS; q += 32) sts(s0 + 4 * q, 1.0f);
             }
-            const uint32_t chunk = static_cast<uint32_t>(a ^ (b & 7)) << 4;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                sts(t_s + (4 * b + k) * 128 + chunk, make_uint4(y[0][k], y[1][k], y[2][k], y[3][k]));
         }
+        worker_sync();
+        // phase B: the next tile's copies go out; codes leave through ldmatrix transposes.  A
+        // warp takes the worker's 16-channel chunks 4 wq..4 wq + 3.  Per chunk, two x2 loads
+        // read four 16x16 matrices; lane t addresses row i = t & 15 of matrix mm = t >> 4 (and
+        // mm + 2 in the second load): tile row 16 (i >> 2) + 4 mm + (i & 3).  Lane t then holds
+        // rows 16 (t & 3)..+15 of channels t / 4 and t / 4 + 8 of the chunk.
+        issue(t + workers);
         const int64_t rp = m.rows_padded;
+        {
+            const int i = lane & 15;
+            const uint32_t ra = 64 * half + 16 * (i >> 2) + 4 * (lane >> 4) + (i & 3);
+            const uint32_t ga = (ra & 3u) | ((ra >> 2) & 4u);   // swizzle key of rows ra and ra + 8
+            const int64_t o0 = d0 + 16 * (lane & 3);
+            // (every lane runs the ldmatrix loads: they are warp-wide; only the stores of lanes
+            // past rows_padded are skipped)
+            const bool any = o0 < rp;
+            const bool vec = o0 + 16 <= rp && ((reinterpret_cast<uintptr_t>(m.out_codes) | static_cast<uintptr_t>(rp)) & 15) == 0;
+            const int ne = !any ? 0 : (rp - o0 < 16 ? static_cast<int>(rp - o0) : 16);
+            uint8_t* const dst0 = m.out_codes + static_cast<int64_t>(cb * kModalixCols + (lane >> 2)) * rp + (any ? o0 : 0);
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const uint32_t c = 4 * wq + cc;
+                const uint32_t a = r_s + ra * 256 + ((c ^ ga ^ (3u * (c >> 3))) << 4);
+                uint32_t v[8];
+                ldsm_x2_trans_b8(a, v[0], v[1], v[2], v[3]);            // rows 16q + 0..7
+                ldsm_x2_trans_b8(a + 8 * 256, v[4], v[5], v[6], v[7]);  // rows 16q + 8..15
+                uint8_t* dst = dst0 + static_cast<int64_t>(16 * c) * rp;
+                if (vec) {
+                    stg128(dst, make_uint4(v[0], v[2], v[4], v[6]));
+                    stg128(dst + 8 * rp, make_uint4(v[1], v[3], v[5], v[7]));
+                } else if (any) {
+                    // (indices fixed at compile time, so that v stays in registers)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        if (e < ne) {
+                            st_global(dst + e, static_cast<uint8_t>(v[2 * (e >> 2)] >> (8 * (e & 3))));
+                            st_global(dst + 8 * rp + e, static_cast<uint8_t>(v[2 * (e >> 2) + 1] >> (8 * (e & 3))));
+                        }
+                    }
+                }
+            }
+        }
         for (int task = hid; task < X::NBS * 16; task += 128) {
             const int bb = task % X::NBS, quad = task / X::NBS;   // scale column, 4 output channels
             const int64_t o0 = d0 + 4 * quad;
             if (o0 >= rp) continue;
             float v[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                v[e] = (4 * quad + e < valid_rows)
-                           ? __uint_as_float(lds_u32(s_s + 4 * ((64 * half + 4 * quad + e) * X::NBS + bb)))
-                           : 1.0f;
+            for (int e = 0; e < 4; ++e) v[e] = __uint_as_float(lds_u32(s_s + 4 * ((64 * half + 4 * quad + e) * X::NBS + bb)));
             float* dst = m.out_scales + static_cast<int64_t>(cb * X::NBS + bb) * rp + o0;
             if (o0 + 4 <= rp && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
                 st_global(reinterpret_cast<float4*>(dst), make_float4(v[0], v[1], v[2], v[3]));
@@ -1213,30 +1224,8 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
                 for (int e = 0; e < 4 && o0 + e < rp; ++e) st_global(dst + e, v[e]);
             }
         }
+        // the row and scale tiles are read: the next decode may overwrite them
         worker_sync();
-        // phase C: column tile -> codes, 16 output channels per lane: lanes 4s + l of a
-        // quarter warp take output channels 16l.. of input channels i and i + 16, whose
-        // chunks (q ^ u and q ^ u ^ 4) fill all eight 16-byte bank groups
-        const int q = 4 * half + (lane & 3);                                  // row-tile group of 16
-        const int64_t o0 = d0 + 16 * (lane & 3);
-        const bool seg_full = o0 + 16 <= rp;
-        if (o0 < rp) {
-#pragma unroll 4
-            for (int it = 0; it < 8; ++it) {
-                const int idx = wq * 8 + it;
-                const int i = 32 * (idx >> 2) + 4 * (idx & 3) + 16 * ((lane >> 2) & 1) + (lane >> 3);
-                const uint4 w = lds_v4(t_s + i * 128 + ((q ^ ((i >> 2) & 7)) << 4));
-                uint8_t* dst = m.out_codes + static_cast<int64_t>(cb * kModalixCols + i) * rp + o0;
-                if (seg_full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                    stg128(dst, w);
-                } else {
-                    for (int e = 0; e < 16 && o0 + e < rp; ++e) {
-                        const uint32_t word = e < 4 ? w.x : (e < 8 ? w.y : (e < 12 ? w.z : w.w));
-                        st_global(dst + e, static_cast<uint8_t>(word >> (8 * (e & 3))));
-                    }
-                }
-            }
-        }
     }
     cp_async_wait<0>();
     acc.flush(lane);
