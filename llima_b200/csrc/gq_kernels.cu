@@ -1028,7 +1028,8 @@ struct MxFmt {
     static constexpr int kWarpStaging = 16 * STR + 16;      // + slack for lds128_align2
     static constexpr int kRBytes = 2 * kModalixRows * kModalixCols;   // row tile, both workers
     static constexpr int kSBytes = 2 * kModalixRows * NBS * 4;        // scale tile, both workers
-    static constexpr int kSmem = kRBytes + kSBytes + 8 * kWarpStaging + 8192;   // + alignment
+    // two staging buffers per warp: the next tile's copies land during this tile's work
+    static constexpr int kSmem = kRBytes + kSBytes + 16 * kWarpStaging + 8192;   // + alignment
 };
 
 // Source row of output channel o (inverse of the q/k permutation of
@@ -1070,7 +1071,7 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
             asm volatile("bar.sync 2, 128;" ::: "memory");
         }
     };
-    uint8_t* staging = smem + X::kRBytes + X::kSBytes + warp * X::kWarpStaging;
+    uint8_t* const staging0 = smem + X::kRBytes + X::kSBytes + warp * 2 * X::kWarpStaging;
     __syncthreads();
 
     // a worker visits its tiles in increasing order, so each tensor cursor only moves forward
@@ -1082,8 +1083,12 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
 
     // tile t of the batch: tensor m, row block rb (output channels d0..d0+63), column
     // block cb (256 input channels)
-    auto issue = [&](uint32_t t) {
-        if (t >= b.total_tiles) return;
+    // (every call commits one cp.async group, empty past the last tile)
+    auto issue = [&](uint32_t t, uint8_t* staging) {
+        if (t >= b.total_tiles) {
+            cp_async_commit();
+            return;
+        }
         const GqModalix& m = seek(c_issue, t);
         const uint32_t lt = t - m.tile_begin;
         const uint32_t rb = fast_div(lt, m.ncol_mul, m.ncol_shift), cb = lt - rb * m.n_col_tiles;
@@ -1111,8 +1116,14 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
 
     const uint32_t workers = 2 * gridDim.x;
     uint32_t t = 2 * blockIdx.x + half;
-    issue(t);
-    for (; t < b.total_tiles; t += workers) {
+    int buf = 0;
+    issue(t, staging0);
+    for (; t < b.total_tiles; t += workers, buf ^= 1) {
+        // the next tile's copies go to the other buffer (its last reader, this warp's
+        // decode two tiles back, is done), then this tile's group is waited for
+        __syncwarp();
+        issue(t + workers, staging0 + (buf ^ 1) * X::kWarpStaging);
+        uint8_t* const staging = staging0 + buf * X::kWarpStaging;
         const GqModalix& m = seek(c_tile, t);
         acc.retarget(m.diag, lane);
         const uint32_t lt = t - m.tile_begin;
@@ -1122,7 +1133,7 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
         // rows of this tile below `rows` (0..64)
         const int valid_rows = d0 >= rows ? 0 : (rows - d0 < kModalixRows ? static_cast<int>(rows - d0) : kModalixRows);
         const int shift = static_cast<int>((cb * X::SEG) & 15);   // row starts are 16-byte aligned
-        cp_async_wait<0>();
+        cp_async_wait<1>();
         __syncwarp();
         // phase A: decode this warp's 16 rows into the row tile / scale tile
         if constexpr (X::K) {
@@ -1169,12 +1180,11 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
             }
         }
         worker_sync();
-        // phase B: the next tile's copies go out; codes leave through ldmatrix transposes.  A
+        // phase B: codes leave through ldmatrix transposes.  A
         // warp takes the worker's 16-channel chunks 4 wq..4 wq + 3.  Per chunk, two x2 loads
         // read four 16x16 matrices; lane t addresses row i = t & 15 of matrix mm = t >> 4 (and
         // mm + 2 in the second load): tile row 16 (i >> 2) + 4 mm + (i & 3).  Lane t then holds
         // rows 16 (t & 3)..+15 of channels t / 4 and t / 4 + 8 of the chunk.
-        issue(t + workers);
         const int64_t rp = m.rows_padded;
         {
             const int i = lane & 15;
