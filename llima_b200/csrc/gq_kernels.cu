@@ -1197,45 +1197,60 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
             const bool vec = o0 + 16 <= rp && ((reinterpret_cast<uintptr_t>(m.out_codes) | static_cast<uintptr_t>(rp)) & 15) == 0;
             const int ne = !any ? 0 : (rp - o0 < 16 ? static_cast<int>(rp - o0) : 16);
             uint8_t* const dst0 = m.out_codes + static_cast<int64_t>(cb * kModalixCols + (lane >> 2)) * rp + (any ? o0 : 0);
+            // all shared reads of the tile first (codes through ldmatrix, this thread's scale
+            // quads), then the block barrier that frees the row and scale tiles for the next
+            // decode, then the global stores, which so overlap the other warps' work
+            constexpr int kNT = X::NBS * 16 / 128;   // scale quads per thread
+            uint32_t v[4][8];
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
                 const uint32_t c = 4 * wq + cc;
                 const uint32_t a = r_s + ra * 256 + ((c ^ ga ^ (3u * (c >> 3))) << 4);
-                uint32_t v[8];
-                ldsm_x2_trans_b8(a, v[0], v[1], v[2], v[3]);            // rows 16q + 0..7
-                ldsm_x2_trans_b8(a + 8 * 256, v[4], v[5], v[6], v[7]);  // rows 16q + 8..15
-                uint8_t* dst = dst0 + static_cast<int64_t>(16 * c) * rp;
+                ldsm_x2_trans_b8(a, v[cc][0], v[cc][1], v[cc][2], v[cc][3]);            // rows 16q + 0..7
+                ldsm_x2_trans_b8(a + 8 * 256, v[cc][4], v[cc][5], v[cc][6], v[cc][7]);  // rows 16q + 8..15
+            }
+            float sv[kNT][4];
+#pragma unroll
+            for (int j = 0; j < kNT; ++j) {
+                const int task = hid + 128 * j;
+                const int bb = task % X::NBS, quad = task / X::NBS;   // scale column, 4 output channels
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    sv[j][e] = __uint_as_float(lds_u32(s_s + 4 * ((64 * half + 4 * quad + e) * X::NBS + bb)));
+            }
+            // the row and scale tiles are read: the next decode may overwrite them
+            worker_sync();
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                uint8_t* dst = dst0 + static_cast<int64_t>(16 * (4 * wq + cc)) * rp;
                 if (vec) {
-                    stg128(dst, make_uint4(v[0], v[2], v[4], v[6]));
-                    stg128(dst + 8 * rp, make_uint4(v[1], v[3], v[5], v[7]));
+                    stg128(dst, make_uint4(v[cc][0], v[cc][2], v[cc][4], v[cc][6]));
+                    stg128(dst + 8 * rp, make_uint4(v[cc][1], v[cc][3], v[cc][5], v[cc][7]));
                 } else if (any) {
                     // (indices fixed at compile time, so that v stays in registers)
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         if (e < ne) {
-                            st_global(dst + e, static_cast<uint8_t>(v[2 * (e >> 2)] >> (8 * (e & 3))));
-                            st_global(dst + 8 * rp + e, static_cast<uint8_t>(v[2 * (e >> 2) + 1] >> (8 * (e & 3))));
+                            st_global(dst + e, static_cast<uint8_t>(v[cc][2 * (e >> 2)] >> (8 * (e & 3))));
+                            st_global(dst + 8 * rp + e, static_cast<uint8_t>(v[cc][2 * (e >> 2) + 1] >> (8 * (e & 3))));
                         }
                     }
                 }
             }
-        }
-        for (int task = hid; task < X::NBS * 16; task += 128) {
-            const int bb = task % X::NBS, quad = task / X::NBS;   // scale column, 4 output channels
-            const int64_t o0 = d0 + 4 * quad;
-            if (o0 >= rp) continue;
-            float v[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) v[e] = __uint_as_float(lds_u32(s_s + 4 * ((64 * half + 4 * quad + e) * X::NBS + bb)));
-            float* dst = m.out_scales + static_cast<int64_t>(cb * X::NBS + bb) * rp + o0;
-            if (o0 + 4 <= rp && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                st_global(reinterpret_cast<float4*>(dst), make_float4(v[0], v[1], v[2], v[3]));
-            } else {
-                for (int e = 0; e < 4 && o0 + e < rp; ++e) st_global(dst + e, v[e]);
+            for (int j = 0; j < kNT; ++j) {
+                const int task = hid + 128 * j;
+                const int bb = task % X::NBS, quad = task / X::NBS;
+                const int64_t s0 = d0 + 4 * quad;
+                if (s0 >= rp) continue;
+                float* dst = m.out_scales + static_cast<int64_t>(cb * X::NBS + bb) * rp + s0;
+                if (s0 + 4 <= rp && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    st_global(reinterpret_cast<float4*>(dst), make_float4(sv[j][0], sv[j][1], sv[j][2], sv[j][3]));
+                } else {
+                    for (int e = 0; e < 4 && s0 + e < rp; ++e) st_global(dst + e, sv[j][e]);
+                }
             }
         }
-        // the row and scale tiles are read: the next decode may overwrite them
-        worker_sync();
     }
     cp_async_wait<0>();
     acc.flush(lane);
