@@ -340,11 +340,33 @@ __device__ __forceinline__ uint32_t lds16(const uint8_t* p) {
 }
 
 // 16 bytes from a 2-byte-aligned shared address: five aligned words and funnel shifts.
+// SMEM_LD selects how the words are read: explicit shared loads at the word-aligned shared
+// address (the fused layout writer's decode, whose staging reads measured faster so:
+// Q6_K 1.644 -> 1.580 ms per Llama-3-8B set), or plain loads through the word pointer (the
+// conversion kernels, where the explicit form measured slower: Q8_0 0.368 -> 0.420 ms on
+// the Qwen2.5-7B set).
+template <bool SMEM_LD = false>
 __device__ __forceinline__ uint4 lds128_align2(const uint8_t* p) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-    const uint32_t sh = static_cast<uint32_t>(a & 3u) * 8u;
-    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+    uint32_t w0, w1, w2, w3, w4, sh;
+    if constexpr (SMEM_LD) {
+        const uint32_t a = smem_u32addr(p);
+        const uint32_t b = a & ~3u;
+        sh = (a & 3u) * 8u;
+        asm volatile("ld.shared.u32 %0, [%5];\n\tld.shared.u32 %1, [%5+4];\n\tld.shared.u32 %2, [%5+8];\n\t"
+                     "ld.shared.u32 %3, [%5+12];\n\tld.shared.u32 %4, [%5+16];"
+                     : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3), "=r"(w4)
+                     : "r"(b)
+                     : "memory");
+    } else {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+        sh = static_cast<uint32_t>(a & 3u) * 8u;
+        w0 = w[0];
+        w1 = w[1];
+        w2 = w[2];
+        w3 = w[3];
+        w4 = w[4];
+    }
     uint4 r;
     r.x = __funnelshift_r(w0, w1, sh);
     r.y = __funnelshift_r(w1, w2, sh);

@@ -521,8 +521,8 @@ __device__ __forceinline__ void process_q6k(const GqDesc& D, int64_t unit0, int 
         // value 128*hh + 32*g + j: nibble of ql[64hh + 32(g&1) + j] (low for g<2),
         // high bits 2g..2g+1 of qh[32hh + j] (ggml_quant.py:274-308)
         const int hh = kb >> 3, g = (kb >> 1) & 3, j0 = 16 * (kb & 1);
-        const uint4 ql = lds128_align2(sbp + 64 * hh + 32 * (g & 1) + j0);
-        const uint4 qh = lds128_align2(sbp + 128 + 32 * hh + j0);
+        const uint4 ql = lds128_align2<(MODE & kOutSmem) != 0>(sbp + 64 * hh + 32 * (g & 1) + j0);
+        const uint4 qh = lds128_align2<(MODE & kOutSmem) != 0>(sbp + 128 + 32 * hh + j0);
         const int qls = 4 * (g >> 1), qhs = 2 * g;
         const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w};
         const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
@@ -573,7 +573,7 @@ __device__ __forceinline__ void process_q0(const GqDesc& D, int64_t unit0, int n
         const int h = c & 1;
         if (b >= nunits) continue;
         const uint8_t* bp = tile + UB * b;
-        const uint4 xv = lds128_align2(bp + 2 + (Q4 ? 0 : 16 * h));
+        const uint4 xv = lds128_align2<(MODE & kOutSmem) != 0>(bp + 2 + (Q4 ? 0 : 16 * h));
         uint32_t x[4] = {xv.x, xv.y, xv.z, xv.w};
         if (Q4) {
             // value j: low nibble of byte j, value 16+j: high nibble; int4 byte = (n-8)&15 = n^8
@@ -645,7 +645,7 @@ __device__ __forceinline__ void process_q32(const GqDesc& D, int64_t unit0, int 
     const float d = h2f(lds16(bp));
     const float m = kAsym ? h2f(lds16(bp + 2)) : 0.0f;
     const uint32_t qh = kQ5 ? lds32_align2(bp + QH) : 0u;
-    const uint4 nb = lds128_align2(bp + QS);
+    const uint4 nb = lds128_align2<(MODE & kOutSmem) != 0>(bp + QS);
     const uint32_t nw[4] = {nb.x, nb.y, nb.z, nb.w};
     uint32_t q[8];   // values 0..15: low nibbles of bytes 0..15; 16..31: high nibbles
 #pragma unroll
@@ -723,7 +723,7 @@ __device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int 
             mn = sbyte >> 4;
             d = h2f(lds16(sbp + 80));
             dmin = h2f(lds16(sbp + 82));
-            const uint4 x = lds128_align2(sbp + 16 + 32 * h + b0);
+            const uint4 x = lds128_align2<(MODE & kOutSmem) != 0>(sbp + 16 + 32 * h + b0);
             const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) q[i] = (xw[i] >> (2 * j)) & 0x03030303u;
@@ -736,8 +736,8 @@ __device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int 
             const int top = (sp[8 + (kb & 3)] >> (2 * (kb >> 2))) & 3;
             sc = (low | (top << 4)) - 32;
             d = h2f(lds16(sbp + 108));
-            const uint4 x = lds128_align2(sbp + 32 + 32 * h + b0);
-            const uint4 hm = lds128_align2(sbp + b0);
+            const uint4 x = lds128_align2<(MODE & kOutSmem) != 0>(sbp + 32 + 32 * h + b0);
+            const uint4 hm = lds128_align2<(MODE & kOutSmem) != 0>(sbp + b0);
             const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
             const uint32_t hw[4] = {hm.x, hm.y, hm.z, hm.w};
 #pragma unroll
@@ -1050,8 +1050,10 @@ __global__ void __launch_bounds__(256, 2) gq_modalix_kernel(const __grid_constan
     __shared__ float recip[17];
     if (threadIdx.x < 17) recip[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, static_cast<float>(threadIdx.x)) : 0.0f;
     // the row tile starts on an 8 KiB boundary: its swizzle key (shared-address bits 8, 9
-    // and 12) is then made of bits 0, 1 and 4 of the row index
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 8191) & ~uintptr_t(8191));
+    // and 12) is then made of bits 0, 1 and 4 of the row index (the offset is added to the
+    // shared pointer, not formed through an integer, so that loads through the staging
+    // pointers stay shared loads)
+    uint8_t* smem = smem_raw + ((8192u - (smem_u32addr(smem_raw) & 8191u)) & 8191u);
     uint8_t* rtile = smem;                                         // 128 rows x 256 bytes
     float* stile = reinterpret_cast<float*>(smem + X::kRBytes);    // 128 rows x NBS
     const uint32_t r_s = smem_u32addr(rtile);
