@@ -209,9 +209,13 @@ __device__ unsigned int gq_kernel_errors;
 //   EL = w & 0x000F000F   low nibbles of b0, b2  (value << 0)
 //   OL = w & 0x0F000F00   low nibbles of b1, b3  (value << 8)
 //   EH = w & 0x00F000F0   high nibbles of b0, b2 (value << 4)
-//   OH = w & 0xF000F000   high nibbles of b1, b3 (value << 12; Q5_K: shifted down)
+//   OH = w & 0xF000F000   high nibbles of b1, b3 (value << 12)
 // so the same masked words feed the min/max scan and the requantization: q*sf + rm is
-// one IMAD per two codes (mad.hi undoes the << 8 / << 12 for free).
+// one IMAD per two codes (mad.hi undoes the << 8 / << 12 for free).  Q5_K first builds,
+// once per word, the 5-bit codes of both blocks as bytes (L: low nibbles with the block-2g
+// fifth bits, H: high nibbles with the block-2g+1 fifth bits, each merge one IMAD); its
+// layouts are then L and H masked to bytes 0, 2 (<< 0) and 1, 3 (<< 8), and both blocks
+// take the low block's arithmetic.
 // ---------------------------------------------------------------------------------------
 
 // Codes of one block side from its two 16-bit-lane words (E holds bytes 0 and 2, O bytes
@@ -232,8 +236,8 @@ __device__ __forceinline__ uint32_t requant_word_general(uint32_t q4, const Requ
     return requant_word_slow(q4, p.sf, p.rm, -128, 127);
 }
 
-// The 32 code bytes of one group (and Q5_K's fifth-bit bytes, pre-shifted so that bit 0
-// of each byte is the fifth bit of the low-nibble block).
+// The 32 code bytes of one group: Q4_K the raw nibble words; Q5_K the 5-bit codes, w[i] of
+// block 2g and h[i] of block 2g+1, one code per byte.
 template <bool Q5>
 struct GroupWords {
     uint32_t w[8];
@@ -251,11 +255,11 @@ __device__ __forceinline__ void group_layouts(const GroupWords<Q5>& q, int i, ui
         eh = w & 0x00F000F0u;
         oh = w & 0xF000F000u;
     } else {
-        const uint32_t t = q.h[Q5 ? i : 0], t4 = t << 4;
-        el = (w & 0x000F000Fu) | (t4 & 0x00100010u);
-        ol = (w & 0x0F000F00u) | (t4 & 0x10001000u);
-        eh = (w & 0x00F000F0u) | ((t << 7) & 0x01000100u);
-        oh = ((w >> 12) & 0x000F000Fu) | ((t >> 5) & 0x00100010u);
+        const uint32_t h = q.h[Q5 ? i : 0];
+        el = w & 0x00FF00FFu;
+        ol = w & 0xFF00FF00u;
+        eh = h & 0x00FF00FFu;
+        oh = h & 0xFF00FF00u;
     }
 }
 
@@ -329,7 +333,8 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
                                             const float* recip) {
     constexpr int UB = Q5 ? 176 : 144;
     constexpr int QS = Q5 ? 48 : 16;   // offset of the nibble bytes
-    constexpr int kOHShift = Q5 ? 0 : 12;
+    constexpr int kEHShift = Q5 ? 0 : 4;    // high block: layout shift of bytes 0, 2
+    constexpr int kOHShift = Q5 ? 8 : 12;   // and of bytes 1, 3
     const int g = lane & 3;
     const uint32_t sel = (g & 1) ? 0x4432u : 0x4410u;
 
@@ -355,11 +360,16 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
         q.w[4] = qb.x; q.w[5] = qb.y; q.w[6] = qb.z; q.w[7] = qb.w;
         if (Q5) {
             // fifth bit of block k is bit k of qh[j] (ggml_quant.py:311-349): bit 2g for the
-            // low nibbles, 2g+1 for the high nibbles
+            // low nibbles, 2g+1 for the high nibbles; the bits are disjoint from the
+            // nibbles, so each merge is a multiply-add
             const uint4 ha = lds128(sbp + 16), hb = lds128(sbp + 32);
             const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) q.h[Q5 ? i : 0] = hw[i] >> (2 * g);
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t t = hw[i] >> (2 * g), w = q.w[i];
+                q.w[i] = (t & 0x01010101u) * 16u + (w & 0x0F0F0F0Fu);
+                q.h[Q5 ? i : 0] = (t & 0x02020202u) * 8u + ((w >> 4) & 0x0F0F0F0Fu);
+            }
         }
     }
 
@@ -390,8 +400,8 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
             mnOH = vmin16(mnOH, a3, c3); mxOH = vmax16(mxOH, a3, c3);
         }
         const uint32_t aminL = vmin16(mnEL, mnOL >> 8), amaxL = vmax16(mxEL, mxOL >> 8);
-        const uint32_t aminH = vmin16(mnEH >> 4, mnOH >> kOHShift);
-        const uint32_t amaxH = vmax16(mxEH >> 4, mxOH >> kOHShift);
+        const uint32_t aminH = vmin16(mnEH >> kEHShift, mnOH >> kOHShift);
+        const uint32_t amaxH = vmax16(mxEH >> kEHShift, mxOH >> kOHShift);
         const int qminL = min(aminL & 0xFFFF, aminL >> 16), qmaxL = max(amaxL & 0xFFFF, amaxL >> 16);
         const int qminH = min(aminH & 0xFFFF, aminH >> 16), qmaxH = max(amaxH & 0xFFFF, amaxH >> 16);
 
@@ -413,12 +423,13 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             // low nibbles: EL*sf + K and high32(OL * (sf << 24)) + K; high nibbles:
-            // (EH*sf + 16K) >> 4 and high32(OH * (sf << 20)) + K (Q5_K: OH*sf + K); the
-            // low bytes of the 16-bit lanes are the codes (the bias has a zero low byte)
+            // (EH*sf + 16K) >> 4 and high32(OH * (sf << 20)) + K (Q5_K: as the low ones);
+            // the low bytes of the 16-bit lanes are the codes (the bias has a zero low byte)
             uint32_t el, ol, eh, oh;
             group_layouts(q, i, el, ol, eh, oh);
             lo[i] = codes_word(el * sfiL + KL, mad_hi(ol, sfiL << 24, KL));
-            hi[i] = codes_word((eh * sfiH + (KH << 4)) >> 4, Q5 ? oh * sfiH + KH : mad_hi(oh, sfiH << 20, KH));
+            hi[i] = Q5 ? codes_word(eh * sfiH + KH, mad_hi(oh, sfiH << 24, KH))
+                       : codes_word((eh * sfiH + (KH << 4)) >> 4, mad_hi(oh, sfiH << 20, KH));
         }
         uint8_t* base = D.codes + off;
         if ((MODE & kOutSmem) == 0 && (reinterpret_cast<uintptr_t>(D.codes) & 31u) == 0) {
@@ -488,7 +499,7 @@ __device__ __forceinline__ void process_k45(const GqDesc& D, int64_t unit0, int 
             uint32_t el, ol, eh, oh;
             group_layouts(q, i, el, ol, eh, oh);
             const uint32_t ql = codes_word(el, ol >> 8);
-            const uint32_t qh = codes_word(eh >> 4, oh >> kOHShift);
+            const uint32_t qh = codes_word(eh >> kEHShift, oh >> kOHShift);
             stg128f(vdst + 4 * i, __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 0))), dmL),
                     __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 1))), dmL),
                     __fsub_rn(__fmul_rn(dsL, static_cast<float>(byte_of(ql, 2))), dmL),
