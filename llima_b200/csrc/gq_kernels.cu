@@ -54,6 +54,9 @@ namespace gq {
 #endif
 // Q5_K with per-lane copies (8-layer Qwen2.5-7B Q5_K set, GB/s): 1 sub-tile x 4 stages
 // 3930, 2 x 3 4240, 3 x 3 4387, 4 x 2 4484-4493, 5 x 2 4487, 4 x 3 at 6 warps 4052.
+// Re-checked with bulk copies and the byte-form 5-bit codes (96 registers; whole Qwen2.5-7B
+// Q5_K set, ms): 5 x 2 at 8 warps 2.17-2.18, 4 x 2 2.20-2.21, 6-warp CTAs three per SM
+// 4 x 2 2.35-2.37, 3 x 2 2.38-2.39.
 #ifndef GQ_Q5K_SUB
 #define GQ_Q5K_SUB 5
 #endif
