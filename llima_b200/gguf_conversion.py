@@ -234,8 +234,20 @@ def convert_gguf_file(path, names=None, force_float: bool = False, permute_qk: b
         if fmt not in _GPU_TYPES:
             raise NotImplementedError(f"GGML type {fmt} is not handled by the B200 GGUF path")
         jobs.append((t, fmt, heads))
+    for (t, _, _), (scales, w, d) in zip(jobs, convert_tensors(jobs, force_float, device)):
+        if d is not None:
+            requant_warning(*d)
+        out[t.name] = (scales, w)
+    return out
+
+
+def convert_tensors(jobs, force_float: bool = False, device: int | None = None) -> list:
+    """GGUF reader tensors ``[(tensor, fmt, perm_heads)]`` (quantized types on the path) in
+    one host-buffer call: ``[(scales | None, weights, (round_error, clip_error) | None)]`` in
+    order, each as ``load_tensor`` returns it, with the requantization diagnostics handed
+    back instead of logged."""
     if not jobs:
-        return out
+        return []
     recs = (N.Tensor * len(jobs))()
     diags = (N.Diag * len(jobs))()
     results = []
@@ -253,25 +265,27 @@ def convert_gguf_file(path, names=None, force_float: bool = False, permute_qk: b
         if force_float:
             values = _host_empty((rows, cols), np.float32)
             r.values = _host_ptr(values)
-            results.append((t.name, fmt, shape, raw, None, values))
+            results.append((fmt, shape, raw, None, values))
         else:
             codes = _host_empty((rows, cols), np.int8)
             scales = _host_empty((rows * cols // f.block_values, 1), np.float32)
             r.codes, r.scales = _host_ptr(codes), _host_ptr(scales)
-            results.append((t.name, fmt, shape, raw, scales, codes))
+            results.append((fmt, shape, raw, scales, codes))
         recs[i] = r
     dev = _device() if device is None else device
     mask = N.OUT_F32 if force_float else N.OUT_CODES
     N.check(N.lib().gq_convert_host(_session(dev), recs, len(jobs), mask, diags), "gq_convert_host")
-    for (name, fmt, shape, _raw, scales, w), dg in zip(results, diags):
+    out = []
+    for (fmt, shape, _raw, scales, w), dg in zip(results, diags):
         if force_float:
-            out[name] = (None, w.reshape(shape))
+            out.append((None, w.reshape(shape), None))
             continue
+        d = None
         if FORMATS[fmt].asymmetric:
-            requant_warning(np.array([dg.round_err_bits], dtype=np.uint32).view(np.float32)[0], np.int16(dg.clip_err))
+            d = (np.array([dg.round_err_bits], dtype=np.uint32).view(np.float32)[0], np.int16(dg.clip_err))
         if fmt == "Q4_0":
             w = w.view(np.uint8).view(int4)
-        out[name] = (scales, w.reshape(shape))
+        out.append((scales, w.reshape(shape), d))
     return out
 
 
@@ -351,18 +365,91 @@ def unpack_gguf_tensor(gguf_tensor, force_float: bool):
     return load_tensor(gguf_tensor, force_float, 0)
 
 
-class GgufReaderProxy:
-    """``GgufReaderProxy`` (gguf_conversion.py:179-205) with the B200 decode."""
+_READAHEAD_MB_DEFAULT = 1024
 
-    def __init__(self, path: Path | str):
+
+def _readahead_bytes() -> int:
+    return max(0, int(os.environ.get("LLIMA_B200_READAHEAD_MB", str(_READAHEAD_MB_DEFAULT)))) << 20
+
+
+class GgufReaderProxy:
+    """``GgufReaderProxy`` (gguf_conversion.py:179-205) with the B200 decode.
+
+    ``load_tensor`` of a quantized tensor converts it together with the quantized tensors
+    that follow it in the file, up to ``LLIMA_B200_READAHEAD_MB`` (default 1024) MB of GGUF
+    bytes, in one host-buffer call, so that the host copies, transfers and kernels of
+    successive tensors overlap as in ``convert_gguf_file``.  The tensors read ahead wait in
+    the proxy until their own ``load_tensor`` call hands them out (the requantization
+    warning is logged then, per call, as the reference logs it), so a loader that asks for
+    tensors one at a time in about file order gets whole-file throughput.  At most four
+    times the read-ahead budget of results waits at once (the oldest is dropped first, and
+    converted again if it is asked for later).  ``perm_heads_of(name)`` gives the q/k head
+    count the caller will ask for a tensor with (``install`` sets it from the model's
+    config); while it is None, ``attn_q`` / ``attn_k`` tensors are not read ahead.
+    ``LLIMA_B200_READAHEAD_MB=0`` converts each tensor on its own."""
+
+    def __init__(self, path: Path | str, perm_heads_of=None):
+        from collections import OrderedDict
         from gguf import GGUFReader
         self._gguf_reader = GGUFReader(path)
         self._tensor_map = {x.name: idx for idx, x in enumerate(self._gguf_reader.tensors)}
+        self.perm_heads_of = perm_heads_of
+        self._ahead: OrderedDict = OrderedDict()   # (name, force_float, heads) -> (scales, weights, diag, bytes)
+        self._ahead_bytes = 0
+        self._lock = threading.Lock()
+
+    def _heads(self, name: str):
+        if self.perm_heads_of is not None:
+            return int(self.perm_heads_of(name))
+        if name.endswith(("attn_q.weight", "attn_q.bias", "attn_k.weight", "attn_k.bias")):
+            return None
+        return 0
 
     def load_tensor(self, tensor_name: str, force_float: bool, perm_heads: int = 0):
         assert tensor_name in self._tensor_map, f"Tensor {tensor_name} not exist in tensor map."
-        gguf_tensor = self._gguf_reader.get_tensor(self._tensor_map[tensor_name])
-        return load_tensor(gguf_tensor, force_float, perm_heads)
+        key = (tensor_name, bool(force_float), int(perm_heads))
+        with self._lock:
+            hit = self._ahead.pop(key, None)
+            if hit is not None:
+                self._ahead_bytes -= hit[3]
+                if hit[2] is not None:
+                    requant_warning(*hit[2])
+                return hit[0], hit[1]
+            idx = self._tensor_map[tensor_name]
+            gguf_tensor = self._gguf_reader.get_tensor(idx)
+            budget = _readahead_bytes()
+            fmt = _type_name(gguf_tensor.tensor_type)
+            if budget == 0 or fmt not in _GPU_TYPES or int(gguf_tensor.n_elements) == 0:
+                return load_tensor(gguf_tensor, force_float, perm_heads)
+            jobs = [(gguf_tensor, fmt, int(perm_heads))]
+            keys = [key]
+            total = int(gguf_tensor.n_bytes)
+            tensors = self._gguf_reader.tensors
+            for j in range(idx + 1, len(tensors)):
+                if total >= budget:
+                    break
+                t = tensors[j]
+                f = _type_name(t.tensor_type)
+                if f not in _GPU_TYPES or int(t.n_elements) == 0:
+                    continue
+                heads = self._heads(t.name)
+                k = (t.name, bool(force_float), heads)
+                if heads is None or k in self._ahead:
+                    continue
+                jobs.append((t, f, heads))
+                keys.append(k)
+                total += int(t.n_bytes)
+            res = convert_tensors(jobs, force_float)
+            for k, (sc, w, d) in zip(keys[1:], res[1:]):
+                nb = w.nbytes + (sc.nbytes if sc is not None else 0)
+                self._ahead[k] = (sc, w, d, nb)
+                self._ahead_bytes += nb
+            while self._ahead and self._ahead_bytes > 4 * budget:
+                self._ahead_bytes -= self._ahead.popitem(last=False)[1][3]
+        sc, w, d = res[0]
+        if d is not None:
+            requant_warning(*d)
+        return sc, w
 
     def get_fields(self) -> dict:
         return dict(self._gguf_reader.fields.items())
@@ -373,6 +460,17 @@ class GgufReaderProxy:
             t = self._gguf_reader.get_tensor(idx)
             info[name] = {"gguf_type": t.tensor_type, "shape": tuple(t.shape[::-1])}
         return info
+
+
+def _qk_heads(model, name: str) -> int:
+    """Head count of the llama q/k permutation ``GgufModel.load_weight`` applies to a tensor
+    (gguf_conversion.py:285-300), 0 for the others."""
+    if model._need_permute_qk_proj:
+        if name.endswith(("attn_q.weight", "attn_q.bias")):
+            return int(model.model_config["num_attention_heads"])
+        if name.endswith(("attn_k.weight", "attn_k.bias")):
+            return int(model.model_config["num_key_value_heads"])
+    return 0
 
 
 def _rebuild_model(gguf_module: str, cls_module: str, qualname: str, state: dict):
@@ -439,13 +537,11 @@ def install(module=None):
             name = self.convert_hf_weight_name(name)
         if name == "token_embd.weight" and self.__dict__.get("_llima_b200_shape_only"):
             return None, np.empty((int(self.tensor_info[name]["shape"][0]), 0), dtype=np.float32)
-        heads = 0
-        if self._need_permute_qk_proj:
-            if name.endswith(("attn_q.weight", "attn_q.bias")):
-                heads = self.model_config["num_attention_heads"]
-            elif name.endswith(("attn_k.weight", "attn_k.bias")):
-                heads = self.model_config["num_key_value_heads"]
-        return self.gguf_proxy.load_tensor(name, force_float, heads)
+        proxy = self.gguf_proxy
+        if getattr(proxy, "perm_heads_of", 0) is None:
+            # the proxy reads ahead with the head counts this model will ask for
+            proxy.perm_heads_of = functools.partial(_qk_heads, self)
+        return proxy.load_tensor(name, force_float, _qk_heads(self, name))
 
     model_cls.load_weight = load_weight
     return module

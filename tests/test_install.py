@@ -145,6 +145,7 @@ def test_installed_model_config_skips_the_embedding_decode(tmp_path, monkeypatch
         raise AssertionError("a tensor was converted while building the config")
 
     monkeypatch.setattr(G, "convert_host", no_conversion)
+    monkeypatch.setattr(G, "convert_tensors", no_conversion)
     try:
         G.install(gc)
         G.install(gc)                            # a second install wraps nothing twice
