@@ -320,7 +320,7 @@ def gguf_file_e2e(tensors, host_src, layers: int | None = None):
     import shutil
     import numpy as np
     import gguf
-    from llima_b200.gguf_conversion import convert_gguf_file, load_tensor
+    from llima_b200.gguf_conversion import GgufReaderProxy, convert_gguf_file, load_tensor
     keep = [(t, hs) for t, hs in zip(tensors, host_src)
             if layers is None or not t.name.startswith("blk.") or int(t.name.split(".")[1]) < layers]
     total = sum(hs.numel() for _, hs in keep)
@@ -363,19 +363,35 @@ def gguf_file_e2e(tensors, host_src, layers: int | None = None):
                  "tensors": n, "cut": cut,
                  "api": "convert_gguf_file (GGUFReader memory map, one gq_convert_host call)"}
         perm = {t.name: t.perm_heads for t, _ in keep}
+        # GgufModel.load_weight's path: the proxy's load_tensor, one call per quantized
+        # tensor in file order, each result dropped before the next call
+        listing = [rt for rt in gguf.GGUFReader(path).tensors if rt.tensor_type.name not in ("F32", "F16", "BF16")]
+        names = [rt.name for rt in listing]
+        qbytes = sum(int(rt.n_bytes) for rt in listing)
+        del listing
+        proxy = GgufReaderProxy(path, perm_heads_of=lambda n: perm.get(n, 0))
+        t0 = time.perf_counter()
+        for n in names:
+            s_, w_ = proxy.load_tensor(n, False, perm.get(n, 0))
+            del s_, w_
+        dt = time.perf_counter() - t0
+        del proxy
+        dropin = {"value": round(qbytes / dt / 1e9, 3), "unit": "GB/s", "s_per_model": round(dt, 4),
+                  "gguf_bytes": qbytes, "tensors": len(names), "cut": cut,
+                  "readahead_mb": int(os.environ.get("LLIMA_B200_READAHEAD_MB", "1024")),
+                  "api": "GgufReaderProxy.load_tensor (GgufModel.load_weight's path), one call per quantized "
+                         "tensor of a fresh GGUFReader in file order: memory-mapped file in, numpy arrays out"}
+        # the same calls converting each tensor on its own (no read-ahead)
         reader = gguf.GGUFReader(path)
         quant = [rt for rt in reader.tensors if rt.tensor_type.name not in ("F32", "F16", "BF16")]
-        qbytes = sum(int(rt.n_bytes) for rt in quant)
         t0 = time.perf_counter()
         for rt in quant:
             s_, w_ = load_tensor(rt, False, perm.get(rt.name, 0))
             del s_, w_
-        dt = time.perf_counter() - t0
+        dt1 = time.perf_counter() - t0
         del quant, reader
-        dropin = {"value": round(qbytes / dt / 1e9, 3), "unit": "GB/s", "s_per_model": round(dt, 4),
-                  "gguf_bytes": qbytes, "tensors": len(perm), "cut": cut,
-                  "api": "gguf_conversion.load_tensor, one call per quantized tensor of a GGUFReader "
-                         "(GgufModel.load_weight's path): memory-mapped file in, numpy arrays out"}
+        dropin["one_tensor_per_call"] = {"value": round(qbytes / dt1 / 1e9, 3), "unit": "GB/s",
+                                         "s_per_model": round(dt1, 4)}
         return whole, dropin
     finally:
         if os.path.exists(path):
@@ -522,6 +538,47 @@ def work_record(work: list | None) -> dict | None:
     return {"per_rank": [round(w, 4) for w in work], "max": round(max(work), 4), "min": round(min(work), 4),
             "unit": "ms of kernel time per step (sum of the rank's per-format launch events)"}
 
+
+
+def pcie_copy_peak(dev, world: int, nbytes: int = 512 << 20, reps: int = 3) -> dict:
+    """Pinned host <-> device copy bandwidth of this box, the ceiling of the end-to-end figure:
+    host-to-device alone, device-to-host alone and both at once on two streams (each
+    direction's rate while the other runs), timed with CUDA events, every rank at the same
+    time (a multi-GPU run shares the host's memory and I/O path); GB/s summed over ranks."""
+    import torch
+    import torch.distributed as dist
+    hs = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    hd = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    ds_ = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dd = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def run(h2d: bool, d2h: bool) -> tuple[float, float]:
+        ev = {k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for k in ("u", "d")}
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        for key, on, st, fn in (("u", h2d, up, lambda: ds_.copy_(hs, non_blocking=True)),
+                                ("d", d2h, down, lambda: hd.copy_(dd, non_blocking=True))):
+            if not on:
+                continue
+            with torch.cuda.stream(st):
+                ev[key][0].record(st)
+                for _ in range(reps):
+                    fn()
+                ev[key][1].record(st)
+        torch.cuda.synchronize(dev)
+        rate = lambda k: nbytes * reps / (ev[k][0].elapsed_time(ev[k][1]) / 1e3) / 1e9
+        return (rate("u") if h2d else 0.0), (rate("d") if d2h else 0.0)
+
+    run(True, True)   # warm-up
+    h2d_alone, _ = run(True, False)
+    _, d2h_alone = run(False, True)
+    h2d_both, d2h_both = run(True, True)
+    tot = rank_sum([h2d_alone, d2h_alone, h2d_both, d2h_both], world, dev)
+    del hs, hd, ds_, dd
+    return {"h2d_gbs": round(tot[0], 2), "d2h_gbs": round(tot[1], 2), "h2d_gbs_bidir": round(tot[2], 2),
+            "d2h_gbs_bidir": round(tot[3], 2), "bytes_per_copy": nbytes, "copies": reps, "ranks": world}
 
 
 def single_tensor_rate(fmt: str, rows: int, cols: int, dev, world: int, peak: float) -> dict:
@@ -821,7 +878,15 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.all_reduce(agg, op=dist.ReduceOp.SUM)
             dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        # the copy engines' ceiling: the model's bytes in each direction at the rates both
+        # directions reach together on this box
+        pcie = pcie_copy_peak(dev, world)
+        bound_s = max(float(agg[1].item()) / (pcie["h2d_gbs_bidir"] * 1e9),
+                      float(agg[2].item()) / (pcie["d2h_gbs_bidir"] * 1e9))
+        pcie["bound_s_per_model"] = round(bound_s, 4)
+        pcie["frac"] = round(bound_s / e2e_s, 4)
         e2e = {"value": float(agg[0].item()) / e2e_s / 1e9, "unit": "GB/s", "s_per_model": e2e_s,
+               "pcie_roofline": pcie,
                "h2d_bytes_per_step": int(agg[1].item()), "d2h_bytes_per_step": int(agg[2].item()),
                "matches_device": bool(agg[3].item() == world), "api": "gq_convert_host (pinned host buffers)",
                "dropin_pageable": file_dropin,
