@@ -445,3 +445,57 @@ def test_empty_asymmetric_tensor_raises_like_reference():
         convert_host("Q4_K", np.zeros(0, dtype=np.uint8), 0, 256)
     s, w, _ = convert_host("Q6_K", np.zeros(0, dtype=np.uint8), 0, 256)
     assert s.shape == (0, 1) and w.shape == (0, 256)
+
+
+def _force_rare(raw: np.ndarray, fmt: str, rows: int, cols: int, seed: int) -> np.ndarray:
+    """Q4_K / Q5_K bytes in which chosen super-blocks have d = f16(1e-4), every 6-bit scale 1
+    and every min 63, so that |M/S| >= 63 and nearly all their blocks need a scale factor
+    below 0.98 (blocks the fast path leaves).  The density changes by row quarter: 1%, 30%
+    (more such blocks per sub-tile than the kernel's queue holds), 3% with one in seven of
+    them given an inf or NaN d, and none."""
+    f = FORMATS[fmt]
+    u = raw.reshape(-1, f.unit_bytes)
+    rng = np.random.default_rng(seed)
+    quarter = (np.arange(u.shape[0]) // (cols // 256)) * 4 // rows
+    pick = rng.random(u.shape[0]) < np.array([0.01, 0.30, 0.03, 0.0])[quarter]
+    u[pick, 0:2] = np.frombuffer(np.float16(1e-4).tobytes(), np.uint8)
+    u[pick, 4:8] = 0x01
+    u[pick, 8:12] = 0xFF
+    u[pick, 12:16] = 0xF1
+    odd = pick & (quarter == 2) & (rng.random(u.shape[0]) < 1 / 7)
+    u[odd, 0:2] = np.frombuffer(np.array([np.inf], np.float16).tobytes(), np.uint8)
+    u[odd & (rng.random(u.shape[0]) < 0.5), 0:2] = np.frombuffer(np.array([np.nan], np.float16).tobytes(), np.uint8)
+    return raw
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q5_K"])
+@pytest.mark.parametrize("rows,heads", [(2048, 0), (2048, 16), (65536, 0), (65536, 512)])
+def test_rare_blocks_dense_and_sparse(fmt, rows, heads):
+    """Blocks that the integer-scale-factor path leaves, sparse (finished in batches from a
+    per-warp queue), dense (past the queue: finished one warp pass each) and with non-finite
+    constants, at a size that takes the small tiles (2048 rows) and one that takes the large
+    tiles (65536 rows), with and without the q/k head permutation: codes, scales and the
+    diagnostics equal the oracle's bit for bit (the oracle runs on row chunks of whole heads)."""
+    cols = 4096
+    raw = _force_rare(gen_tensor_bytes(fmt, rows * cols, 4321 + rows), fmt, rows, cols, rows + heads)
+    t = _run(fmt, raw, rows, cols, N.OUT_CODES, heads)
+    codes = _codes_np(t)
+    scales = t.scales.cpu().numpy().reshape(rows, cols // 32)
+    f = FORMATS[fmt]
+    row_bytes = cols // 256 * f.unit_bytes
+    chunk = 4096 if heads == 0 else max(4096 // (rows // heads), 1) * (rows // heads)
+    chunk = min(chunk, rows)
+    round_err, clip_err = np.float32(0), 0
+    for r0 in range(0, rows, chunk):
+        part = raw[r0 * row_bytes:(r0 + chunk) * row_bytes]
+        with np.errstate(all="ignore"):
+            s, w, d = O.unpack_tensor(fmt, part.tobytes(), (chunk, cols), log=False)
+        if heads:
+            s, w = O.permute_qk(s, w, chunk // (rows // heads))
+        assert same_bits(codes[r0:r0 + chunk], w), (fmt, rows, heads, r0)
+        assert same_bits(scales[r0:r0 + chunk], s.reshape(chunk, cols // 32)), (fmt, rows, heads, r0)
+        if np.isnan(d.round_error) or d.round_error.view(np.uint32) > round_err.view(np.uint32):
+            round_err = np.float32(d.round_error)
+        clip_err = max(clip_err, int(d.clip_error))
+    r, c = diag_values(t.diag)
+    assert same_bits(np.float32(r), round_err) and int(c) == clip_err
