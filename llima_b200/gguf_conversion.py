@@ -383,7 +383,9 @@ class GgufReaderProxy:
     warning is logged then, per call, as the reference logs it), so a loader that asks for
     tensors one at a time in about file order gets whole-file throughput.  At most four
     times the read-ahead budget of results waits at once (the oldest is dropped first, and
-    converted again if it is asked for later).  ``perm_heads_of(name)`` gives the q/k head
+    converted again if it is asked for later); if the batch fails, the requested tensor is
+    converted on its own, so a call raises only what its own tensor raises.
+    ``perm_heads_of(name)`` gives the q/k head
     count the caller will ask for a tensor with (``install`` sets it from the model's
     config); while it is None, ``attn_q`` / ``attn_k`` tensors are not read ahead.
     ``LLIMA_B200_READAHEAD_MB=0`` converts each tensor on its own."""
@@ -439,7 +441,15 @@ class GgufReaderProxy:
                 jobs.append((t, f, heads))
                 keys.append(k)
                 total += int(t.n_bytes)
-            res = convert_tensors(jobs, force_float)
+            try:
+                res = convert_tensors(jobs, force_float)
+            except Exception:
+                if len(jobs) == 1:
+                    raise
+                # a tensor read ahead that cannot be converted must not fail this call: the
+                # requested tensor alone raises only what its own conversion raises
+                jobs, keys = jobs[:1], keys[:1]
+                res = convert_tensors(jobs, force_float)
             for k, (sc, w, d) in zip(keys[1:], res[1:]):
                 nb = w.nbytes + (sc.nbytes if sc is not None else 0)
                 self._ahead[k] = (sc, w, d, nb)

@@ -9,6 +9,8 @@ proxy).
 * ``attn_q`` / ``attn_k`` are read ahead only with the head count ``perm_heads_of`` gives,
   and a call with another head count or output mode converts afresh;
 * results waiting beyond four budgets are dropped oldest first and converted again later;
+* a batch that fails (a tensor read ahead that cannot be converted) falls back to the
+  requested tensor alone, so a call raises only what its own tensor raises;
 * ``LLIMA_B200_READAHEAD_MB=0`` converts one tensor per call.
 """
 import logging
@@ -154,3 +156,20 @@ def test_read_ahead_off(gguf_file, monkeypatch):
     for n, fmt, *_ in LAYOUT:
         proxy.load_tensor(n, False)
     assert fake.batches == [] and calls == [n for n, *_ in LAYOUT]
+
+
+def test_a_tensor_read_ahead_that_fails_does_not_fail_the_call(gguf_file, monkeypatch):
+    proxy, fake = _proxy(gguf_file, monkeypatch, 1, None)
+
+    def fussy(jobs, force_float=False, device=None):
+        if any(t.name == "blk.1.ffn_down.weight" for t, _, _ in jobs):
+            raise RuntimeError("gq_convert_host: size not supported")
+        return fake(jobs, force_float, device)
+
+    monkeypatch.setattr(G, "convert_tensors", fussy)
+    _, w = proxy.load_tensor("blk.0.attn_v.weight", False)
+    assert int(w.flat[0]) == 30
+    # the batch with the failing tensor was dropped; the requested tensor went alone
+    assert [[b[0] for b in batch] for batch in fake.batches] == [["blk.0.attn_v.weight"]]
+    with pytest.raises(RuntimeError):
+        proxy.load_tensor("blk.1.ffn_down.weight", False)
