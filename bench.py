@@ -547,10 +547,22 @@ def pcie_copy_peak(dev, world: int, nbytes: int = 512 << 20, reps: int = 3) -> d
     time (a multi-GPU run shares the host's memory and I/O path); GB/s summed over ranks."""
     import torch
     import torch.distributed as dist
-    hs = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
-    hd = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
-    ds_ = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    dd = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    try:
+        hs = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+        hd = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+        ds_ = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        dd = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        ok = 1.0
+    except (RuntimeError, MemoryError):
+        hs = hd = ds_ = dd = None
+        ok = 0.0
+    if world > 1:
+        # every rank measures or none does (the measurement's barriers and sums are collective)
+        t = torch.tensor([ok], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok = float(t.item())
+    if ok < 1.0:
+        return {"unavailable": "no room for the pinned copy-test buffers on every rank"}
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
     def run(h2d: bool, d2h: bool) -> tuple[float, float]:
@@ -881,10 +893,11 @@ def run_ours(args, rank, world, local_rank):
         # the copy engines' ceiling: the model's bytes in each direction at the rates both
         # directions reach together on this box
         pcie = pcie_copy_peak(dev, world)
-        bound_s = max(float(agg[1].item()) / (pcie["h2d_gbs_bidir"] * 1e9),
-                      float(agg[2].item()) / (pcie["d2h_gbs_bidir"] * 1e9))
-        pcie["bound_s_per_model"] = round(bound_s, 4)
-        pcie["frac"] = round(bound_s / e2e_s, 4)
+        if "unavailable" not in pcie:
+            bound_s = max(float(agg[1].item()) / (pcie["h2d_gbs_bidir"] * 1e9),
+                          float(agg[2].item()) / (pcie["d2h_gbs_bidir"] * 1e9))
+            pcie["bound_s_per_model"] = round(bound_s, 4)
+            pcie["frac"] = round(bound_s / e2e_s, 4)
         e2e = {"value": float(agg[0].item()) / e2e_s / 1e9, "unit": "GB/s", "s_per_model": e2e_s,
                "pcie_roofline": pcie,
                "h2d_bytes_per_step": int(agg[1].item()), "d2h_bytes_per_step": int(agg[2].item()),
