@@ -32,19 +32,22 @@ namespace gq {
 // ---------------------------------------------------------------------------------------
 
 // Sub-tiles of 8 super-blocks per Q4_K / Q5_K loop iteration, processed one after the
-// other (the per-tile bookkeeping is shared, the registers are not multiplied), and the
-// pipeline depth.  With one bulk copy per tile, fewer and larger tiles win (8-layer cuts,
-// fraction of the measured copy peak, Q4_K / Q5_K): 6 (Q5_K 5) sub-tiles x 2 stages
-// 0.795 / 0.749, 4 x 3 (Q5_K 4 x 2) 0.786 / 0.743, 3 x 4 0.768 / 0.725, 2 x 6 0.737 / 0.697,
-// 4 x 4 at 6-warp CTAs 0.698 / 0.667.
+// other (the per-tile bookkeeping is shared, the registers are not multiplied), the
+// pipeline depth and the warps per CTA.  With one bulk copy per tile, fewer and larger
+// tiles win at 8-warp CTAs (8-layer cuts, fraction of the measured copy peak, Q4_K / Q5_K):
+// 6 (Q5_K 5) sub-tiles x 2 stages 0.795 / 0.749, 4 x 3 (Q5_K 4 x 2) 0.786 / 0.743, 3 x 4
+// 0.768 / 0.725, 2 x 6 0.737 / 0.697, 4 x 4 at 6-warp CTAs 0.698 / 0.667.  Q4_K at 96
+// registers fits two 10-warp CTAs per SM when their tiles are 4 sub-tiles x 2 stages (92 KB
+// of stages per CTA): 20 warps per SM instead of 16 measured 0.4007 against 0.4042 ms on the
+// 8-layer cut and 1.548 against 1.559 ms in the whole 8B step; 3 x 2 tiles at 10 warps 0.412.
 #ifndef GQ_K45_SUB
-#define GQ_K45_SUB 6
+#define GQ_K45_SUB 4
 #endif
 #ifndef GQ_K45_STAGES
 #define GQ_K45_STAGES 2
 #endif
 #ifndef GQ_K45_WARPS
-#define GQ_K45_WARPS 8
+#define GQ_K45_WARPS 10
 #endif
 #ifndef GQ_Q6K_SUB
 #define GQ_Q6K_SUB 2
@@ -56,7 +59,8 @@ namespace gq {
 // 3930, 2 x 3 4240, 3 x 3 4387, 4 x 2 4484-4493, 5 x 2 4487, 4 x 3 at 6 warps 4052.
 // Re-checked with bulk copies and the byte-form 5-bit codes (96 registers; whole Qwen2.5-7B
 // Q5_K set, ms): 5 x 2 at 8 warps 2.17-2.18, 4 x 2 2.20-2.21, 6-warp CTAs three per SM
-// 4 x 2 2.35-2.37, 3 x 2 2.38-2.39.
+// 4 x 2 2.35-2.37, 3 x 2 2.38-2.39; 10-warp CTAs (two per SM only with 3 x 2 tiles) 0.652
+// against 0.640 ms on the 8-layer cut.
 #ifndef GQ_Q5K_SUB
 #define GQ_Q5K_SUB 5
 #endif
@@ -124,6 +128,9 @@ struct FmtSmall : Fmt<TYPE> {
     static constexpr int kTileBytes = Fmt<TYPE>::kUnitBytes * 32;
     static constexpr int kStageBytes = kTileBytes + 16;
     static constexpr int kStages = kQ0 ? 4 : (TYPE == GQ_TYPE_Q4_K ? 3 : 2);
+    // 8-warp CTAs whatever the large tiles use (the measured small-launch configuration)
+    static constexpr int kWarps = 8;
+    static constexpr int kThreads = 32 * kWarps;
 };
 
 // Minimum resident CTAs per SM the Q4_K kernel is compiled for (caps its registers; the
@@ -807,7 +814,7 @@ __device__ __forceinline__ void process_k16(const GqDesc& D, int64_t unit0, int 
 // ---------------------------------------------------------------------------------------
 
 template <int TYPE, int MODE, bool SMALL = false>
-__global__ void __launch_bounds__(Fmt<TYPE>::kThreads,
+__global__ void __launch_bounds__(std::conditional<SMALL, FmtSmall<TYPE>, Fmt<TYPE>>::type::kThreads,
                                   TYPE == GQ_TYPE_Q4_K ? GQ_MIN_BLOCKS : (TYPE == GQ_TYPE_Q5_K ? 2 : 1))
     gq_convert_kernel(const __grid_constant__ GqBatch batch) {
     using F = typename std::conditional<SMALL, FmtSmall<TYPE>, Fmt<TYPE>>::type;
@@ -1302,8 +1309,9 @@ int occupancy(int smem) {
         if (smem > 48 * 1024)
             cudaFuncSetAttribute(gq_convert_kernel<TYPE, MODE, SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  smem);
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gq_convert_kernel<TYPE, MODE, SMALL>,
-                                                          Fmt<TYPE>::kThreads, smem) != cudaSuccess ||
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &occ, gq_convert_kernel<TYPE, MODE, SMALL>,
+                std::conditional<SMALL, FmtSmall<TYPE>, Fmt<TYPE>>::type::kThreads, smem) != cudaSuccess ||
             occ < 1)
             occ = 1;
     }
