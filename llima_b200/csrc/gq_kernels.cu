@@ -1,19 +1,21 @@
 // GGUF block decode + requantization kernels for B200 (sm_100a).
 //
-// One kernel per GGML format (Q8_0, Q4_0, Q4_K, Q5_K, Q6_K), a float pass-through copy,
-// and the standalone requantization scheme.  Each format kernel is a persistent grid of
-// independent warps.  A warp owns a ring of shared-memory stages and streams whole
-// tiles of stored blocks into it with 16-byte cp.async copies (the tile sizes are
-// multiples of 16 bytes, so every copy is aligned and fully coalesced), then decodes
-// the tile from shared memory:
+// One kernel per GGML format (Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K),
+// a float pass-through copy, the standalone requantization scheme and the conversion fused
+// with the Modalix layout.  Each format kernel is a persistent grid of independent warps.
+// A warp owns a ring of shared-memory stages and brings whole tiles of stored blocks into
+// it (tile sizes are multiples of 16 bytes): one bulk copy per tile by the TMA engine,
+// completed on the stage's mbarrier with a bounded wait, or for Q6_K 16-byte cp.async
+// copies of every lane; then it decodes the tile from shared memory.  For the asymmetric
+// formats (Q4_K / Q5_K shown; the others alike):
 //
-//   * "parameter" step: one lane per output block unpacks that block's constants
-//     (6-bit scale/min, f16 super constants), scans its codes for min/max with byte-SIMD
-//     and derives the requantization parameters;
-//   * "apply" step: one lane per 16 output codes, so each warp store instruction writes
-//     512 contiguous bytes; the codes come from packed 16-bit integer arithmetic
-//     (q * sf + rm) whenever the scale factor is an integer (99.5% of blocks on the
-//     benchmark data), else from the per-value f32 formula.
+//   * parameters: each lane takes one 32-byte code group (two blocks), scans its codes for
+//     min / max in 16-bit SIMD lanes, unpacks the blocks' 6-bit scale / min and the f16
+//     super constants, and derives the requantization parameters (requant_fast);
+//   * codes: packed 16-bit integer arithmetic (q * sf + rm, one multiply-add per two codes)
+//     for the blocks with an integer scale factor (99.5% on the benchmark data), written as
+//     one 32-byte store per block; the other blocks are finished by a warp pass each, one
+//     value per lane, with the per-value f32 formula.
 //
 // The fp32 intermediate of dequant -> requant never touches global memory.
 #include <cuda_runtime.h>
