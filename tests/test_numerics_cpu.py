@@ -64,3 +64,16 @@ def test_scale_factor_quotient_keeps_floor_and_threshold(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0, out.stdout
     assert out.stdout.count("violations 0") == 2
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_packed_lane_requantization_is_exact(tmp_path):
+    # gq_kernels.cu (process_k45) computes Q4_K / Q5_K codes with an integer scale factor as
+    # q * sfi + rm in 16-bit lanes of the unshifted code words, the odd bytes by multiply-high,
+    # gathered by a byte permute; this checks every scale factor, offset and pair of codes
+    # sharing an operation against int8(q * sfi + rm).
+    exe = tmp_path / "lane_requant"
+    subprocess.run(["gcc", "-O2", "-o", str(exe), str(HERE / "numerics" / "lane_requant.c")], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout
+    assert "mismatches 0" in out.stdout
