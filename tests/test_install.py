@@ -7,6 +7,9 @@ model into a fresh, unpatched import of the reference module).
 * CPU, with the reference checkout present: a real ``GgufModel`` built on a small GGUF
   file, pickled after ``install``, comes back in a spawned process with the B200 reader
   and ``load_weight``.
+* CPU, with the reference checkout present: the installed ``load_weight`` of a real
+  ``GgufModel`` reads ahead through the proxy with the model's q/k head counts (the
+  conversion replaced by a recorder).
 * GPU: a stand-in module shaped like the reference's (same attribute names and pickling
   hooks) gets the patched ``load_weight``: q/k tensors come back permuted as
   ``_permute_qk_proj`` does it (``gguf_conversion.py:314-332``), equal to the oracle, in
@@ -152,6 +155,48 @@ def test_installed_model_config_skips_the_embedding_decode(tmp_path, monkeypatch
         model = gc.GgufModel(path)
         assert model.model_config == want and model.model_config["vocab_size"] == 64
         assert "_llima_b200_shape_only" not in model.__dict__
+    finally:
+        gc.unpack_gguf_tensor, gc.GgufReaderProxy, gc.GgufModel.load_weight = saved[:3]
+        if saved[3] is None:
+            del gc.GgufModel.__reduce_ex__
+        else:
+            gc.GgufModel.__reduce_ex__ = saved[3]
+        gc.GgufModel.model_config = saved[4]
+
+
+def test_installed_load_weight_reads_ahead_with_the_models_head_counts(tmp_path, monkeypatch):
+    """After install, the reference's own GgufModel.load_weight goes through the proxy's
+    read-ahead: the first call converts the tensors after it in one batch, with the q/k head
+    counts from the model's config (4 and 2 here), and the later calls are handed those
+    results without converting (the conversion is replaced by a recorder: no GPU)."""
+    gc = _import_reference()
+    path = tmp_path / "tiny.gguf"
+    _write_gguf(path)
+    from llima_b200 import gguf_conversion as G
+    saved = (gc.unpack_gguf_tensor, gc.GgufReaderProxy, gc.GgufModel.load_weight,
+             gc.GgufModel.__dict__.get("__reduce_ex__"), gc.GgufModel.__dict__["model_config"])
+    batches = []
+
+    def recorder(jobs, force_float=False, device=None):
+        batches.append([(t.name, heads) for t, _, heads in jobs])
+        out = []
+        for t, _, heads in jobs:
+            shape = tuple(int(x) for x in t.shape[::-1])
+            out.append((np.zeros((int(np.prod(shape)) // 32, 1), np.float32), np.full(shape, heads, np.int8), None))
+        return out
+
+    monkeypatch.setattr(G, "convert_tensors", recorder)
+    monkeypatch.setenv("LLIMA_B200_READAHEAD_MB", "64")
+    try:
+        G.install(gc)
+        model = gc.GgufModel(path)
+        order = [n for n in TENSORS if n != "token_embd.weight"]
+        for n in order:
+            s, w = model.load_weight(n, is_hf_name=False)
+            want = {"blk.0.attn_q.weight": 4, "blk.0.attn_k.weight": 2}.get(n, 0)
+            assert w.shape == TENSORS[n][1:] and int(w.flat[0]) == want, n
+        assert len(batches) == 1
+        assert batches[0] == [(n, {"blk.0.attn_q.weight": 4, "blk.0.attn_k.weight": 2}.get(n, 0)) for n in order]
     finally:
         gc.unpack_gguf_tensor, gc.GgufReaderProxy, gc.GgufModel.load_weight = saved[:3]
         if saved[3] is None:
