@@ -64,7 +64,41 @@ static void check(int qmax, int sfi, int rm, const int q[4], uint32_t other) {
          sfi, rm);
 }
 
+// Q5_K's 5-bit codes as bytes (process_k45): with t = qh_word >> 2g, the low-nibble block's
+// codes are (t & 0x01010101) * 16 + (qs_word & 0x0F0F0F0F) and the high-nibble block's
+// (t & 0x02020202) * 8 + ((qs_word >> 4) & 0x0F0F0F0F); byte j must be nibble | bit << 4 with
+// bit 2g (low) or 2g + 1 (high) of qh byte j (ggml_quant.py:311-349).  Bytes cannot carry
+// into each other (each is at most 31), and every byte pair (qs byte, qh byte) is checked in
+// every byte position against the other positions' bytes at 0x00 and 0xFF.
+static void check_q5_codes(void) {
+  for (int g = 0; g < 4; ++g)
+    for (int pos = 0; pos < 4; ++pos)
+      for (uint32_t fill = 0; fill <= 0xFF; fill += 0xFF)
+        for (uint32_t qs = 0; qs < 256; ++qs)
+          for (uint32_t qh = 0; qh < 256; ++qh) {
+            uint32_t w = 0, h = 0;
+            for (int b = 0; b < 4; ++b) {
+              w |= (b == pos ? qs : fill) << (8 * b);
+              h |= (b == pos ? qh : (fill ^ 0xA5)) << (8 * b);
+            }
+            const uint32_t t = h >> (2 * g);
+            const uint32_t lo = (t & 0x01010101u) * 16u + (w & 0x0F0F0F0Fu);
+            const uint32_t hi = (t & 0x02020202u) * 8u + ((w >> 4) & 0x0F0F0F0Fu);
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t wb = (w >> (8 * b)) & 0xFF, hb = (h >> (8 * b)) & 0xFF;
+              const uint32_t want_lo = (wb & 15) | ((hb >> (2 * g)) & 1) << 4;
+              const uint32_t want_hi = (wb >> 4) | ((hb >> (2 * g + 1)) & 1) << 4;
+              n += 2;
+              if (((lo >> (8 * b)) & 0xFF) != want_lo || ((hi >> (8 * b)) & 0xFF) != want_hi) {
+                if (bad < 5) printf("Q5_K codes g=%d pos=%d qs=%02x qh=%02x byte %d\n", g, pos, qs, qh, b);
+                ++bad;
+              }
+            }
+          }
+}
+
 int main(void) {
+  check_q5_codes();
   const uint32_t others[3] = {0x0000u, 0xFFFFu, 0x5A3Cu};
   for (int qmax = 15; qmax <= 31; qmax += 16) {
     for (int sfi = 1; sfi <= 16; ++sfi) {

@@ -71,7 +71,8 @@ def test_packed_lane_requantization_is_exact(tmp_path):
     # gq_kernels.cu (process_k45) computes Q4_K / Q5_K codes with an integer scale factor as
     # q * sfi + rm in 16-bit lanes of the unshifted code words, the odd bytes by multiply-high,
     # gathered by a byte permute; this checks every scale factor, offset and pair of codes
-    # sharing an operation against int8(q * sfi + rm).
+    # sharing an operation against int8(q * sfi + rm), and the Q5_K code bytes (fifth bits
+    # merged by multiply-add) against nibble | bit << 4 for every qs / qh byte pair.
     exe = tmp_path / "lane_requant"
     subprocess.run(["gcc", "-O2", "-o", str(exe), str(HERE / "numerics" / "lane_requant.c")], check=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True)
